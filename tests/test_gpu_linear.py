@@ -1,0 +1,210 @@
+"""GPU parity of the low-bit path against the CPU oracle (which is pinned to the reference).
+
+* quantize/pack and dequantize: bit-exact.
+* linear (GEMV / tcgen05 GEMM / generic kernels, with bias and rank-r correction):
+  max |y - y_ref| / max |y_ref| <= 1e-2 (the north-star fp16 tolerance), and the mean
+  relative error must stay at fp16-rounding level (<= 2e-3).
+"""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lowbit_ref as ref
+
+pytestmark = pytest.mark.gpu
+TOL_MAX = 1e-2
+TOL_MEAN = 2e-3
+
+
+@pytest.fixture(scope='module')
+def rt():
+    import lowbit_runtime
+    lowbit_runtime.require_cuda()
+    return lowbit_runtime
+
+
+def sha(b):
+    return hashlib.sha256(b).hexdigest()
+
+
+def _quant_cases(z):
+    for key in z.files:
+        if key.endswith('/data'):
+            wname, case, _ = key.split('/')
+            fmt, g = case.split('_g')
+            yield wname, fmt, int(g)
+
+
+def test_quantize_bit_exact_on_reference_fixtures(rt, golden):
+    z = golden('quantize.npz')
+    n_cases = 0
+    for wname, fmt, g in _quant_cases(z):
+        w = torch.from_numpy(z[f'{wname}/w']).cuda()
+        codes, scales = rt.quantize_pack(w, fmt, g)
+        key = f'{wname}/{fmt}_g{g}'
+        assert codes.cpu().numpy().tobytes() == z[key + '/data'].tobytes(), key
+        assert scales.cpu().numpy().tobytes() == z[key + '/scales'].tobytes(), key
+        n, k = w.shape
+        deq = rt.dequantize(fmt, g, n, k, codes, scales)
+        assert sha(deq.cpu().numpy().tobytes()) == str(z[key + '/deq_sha']), key
+        n_cases += 1
+    assert n_cases == 162
+
+
+def baseline_weight(n, k, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    w = (torch.randn(n, k, generator=gen) * 0.02).half()
+    u = (torch.randn(n, 32, generator=gen) * 1e-3).half()
+    v = (torch.randn(32, k, generator=gen) * 1e-3).half()
+    return w, u, v
+
+
+@pytest.mark.parametrize('shape', [(1536, 576), (576, 1536), (8192, 2048), (2048, 8192)])
+def test_quantize_baseline_shapes_match_reference_digests(rt, golden, shape):
+    z = golden('baseline_digests.npz')
+    n, k = shape
+    w, _, _ = baseline_weight(n, k)
+    for fmt, g in (('int8', k), ('int4', 64), ('int4', 128), ('nf4', 64), ('nf4', 128)):
+        if k % g:
+            continue
+        codes, scales = rt.quantize_pack(w.cuda(), fmt, g)
+        key = f'{n}x{k}/{fmt}_g{g}'
+        assert sha(codes.cpu().numpy().tobytes()) == str(z[key + '/data_sha']), key
+        assert sha(scales.cpu().numpy().tobytes()) == str(z[key + '/scales_sha']), key
+        deq = rt.dequantize(fmt, g, n, k, codes, scales)
+        assert sha(deq.cpu().numpy().tobytes()) == str(z[key + '/deq_sha']), key
+
+
+def test_quantize_errors_match_reference(rt):
+    with pytest.raises(ValueError, match='Nonfinite'):
+        rt.quantize_pack(torch.full((2, 16), float('nan'), device='cuda'), 'int4', 16)
+    with pytest.raises(ValueError, match='Nonfinite'):
+        rt.quantize_pack(torch.tensor([[1.0, float('inf')] * 8], device='cuda'), 'nf4', 16)
+    with pytest.raises(ValueError, match='overflows'):
+        rt.quantize_pack(torch.full((1, 8), 3e38, device='cuda'), 'int8', 8)
+
+
+def _compare(y, expected, label):
+    y = y.float().cpu()
+    e = expected.float()
+    assert torch.isfinite(y).all(), label
+    denom = e.abs().max().clamp_min(1e-6)
+    err = (y - e).abs()
+    assert float(err.max() / denom) <= TOL_MAX, (label, float(err.max() / denom))
+    assert float(err.mean() / e.abs().mean().clamp_min(1e-6)) <= TOL_MEAN, (label, float(err.mean()))
+
+
+def _oracle(x, w_shape, fmt, g, data, scales, down=None, up=None, bias=None):
+    return ref.linear(x.cpu(), w_shape, fmt, g, data, scales, down=down, up=up, bias=bias)
+
+
+CASES = [
+    # (n, k, fmt, group)
+    (1536, 576, 'int8', 576), (1536, 576, 'int4', 64), (1536, 576, 'nf4', 64),
+    (576, 1536, 'int4', 128), (576, 1536, 'nf4', 128), (576, 1536, 'int8', 1536),
+    (8192, 2048, 'nf4', 64), (8192, 2048, 'int4', 128), (2048, 8192, 'nf4', 128), (2048, 8192, 'int4', 64),
+    (192, 576, 'nf4', 32), (320, 960, 'int4', 64), (960, 2560, 'nf4', 64), (2048, 2048, 'int8', 2048),
+    (576, 576, 'int8', 64),
+]
+
+
+@pytest.mark.parametrize('n,k,fmt,g', CASES)
+@pytest.mark.parametrize('m', [1, 2, 3, 4, 16, 100, 256])
+def test_linear_matches_oracle_with_correction(rt, n, k, fmt, g, m):
+    w, u, v = baseline_weight(n, k, seed=n + k)
+    group, data, scales = ref.quantize(w.numpy(), fmt, g)
+    gen = torch.Generator().manual_seed(7 + m)
+    x = torch.randn(m, k, generator=gen).half()
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    expected = _oracle(x, (n, k), fmt, group, data, scales, down=v, up=u)
+    y = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda())
+    _compare(y, expected, (n, k, fmt, g, m, rt.linear_select(fmt, group, m, n, k, 32)))
+
+
+@pytest.mark.parametrize('path', ['gemv', 'tc', 'generic'])
+@pytest.mark.parametrize('fmt,g', [('int4', 64), ('nf4', 128), ('int8', 2048), ('int8', 64)])
+def test_every_path_agrees(rt, path, fmt, g):
+    n, k = 2048, 2048
+    m = 4 if path == 'gemv' else 48
+    w, u, v = baseline_weight(n, k, seed=3)
+    group, data, scales = ref.quantize(w.numpy(), fmt, g)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(1)).half()
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(2)) * 0.1).half()
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    expected = _oracle(x, (n, k), fmt, group, data, scales, down=v, up=u, bias=bias)
+    y = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda(), bias=bias.cuda(), path=path)
+    _compare(y, expected, (path, fmt, g))
+
+
+@pytest.mark.parametrize('m', [1, 64, 2048])
+def test_fp16_weights_path(rt, m):
+    n, k = 1024, 576
+    w = (torch.randn(n, k, generator=torch.Generator().manual_seed(5)) * 0.02).half()
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(6)).half()
+    expected = torch.nn.functional.linear(x.float(), w.float()).half()
+    y = rt.linear(x.cuda(), 'fp16', k, n, w.cuda().view(torch.uint8).reshape(-1), None)
+    _compare(y, expected, ('fp16', m))
+
+
+@pytest.mark.parametrize('n,k,fmt,g,rank', [(3, 17, 'int4', 17, 2), (5, 9, 'nf4', 3, 4), (7, 64, 'int8', 32, 7),
+                                            (33, 96, 'nf4', 32, 16), (130, 640, 'int4', 64, 8)])
+def test_ragged_shapes_and_ranks(rt, n, k, fmt, g, rank):
+    w = (torch.randn(n, k, generator=torch.Generator().manual_seed(n)) * 0.05).float()
+    group, data, scales = ref.quantize(w.numpy(), fmt, g)
+    v = (torch.randn(rank, k, generator=torch.Generator().manual_seed(9)) * 1e-2).half()
+    u = (torch.randn(n, rank, generator=torch.Generator().manual_seed(10)) * 1e-2).half()
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    for m in (1, 5, 33):
+        x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).half()
+        expected = _oracle(x, (n, k), fmt, group, data, scales, down=v, up=u)
+        y = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda())
+        _compare(y, expected, (n, k, fmt, g, rank, m))
+
+
+def test_large_prefill_shape_properties(rt):
+    """Full BASELINE prefill size: deterministic, zero-in gives the correction-free zero,
+    and a row sample matches the oracle."""
+    n, k, m = 8192, 2048, 2048
+    w, u, v = baseline_weight(n, k)
+    codes, sc = rt.quantize_pack(w.cuda(), 'nf4', 64)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(11)).half().cuda()
+    y1 = rt.linear(x, 'nf4', 64, n, codes, sc, down=v.cuda(), up=u.cuda())
+    y2 = rt.linear(x, 'nf4', 64, n, codes, sc, down=v.cuda(), up=u.cuda())
+    assert torch.equal(y1, y2)
+    zero = rt.linear(torch.zeros_like(x), 'nf4', 64, n, codes, sc, down=v.cuda(), up=u.cuda())
+    assert int(zero.abs().max().item()) == 0
+    rows = torch.arange(0, m, 97)
+    data, scales = codes.cpu().numpy().tobytes(), sc.cpu().numpy().tobytes()
+    expected = _oracle(x[rows].cpu(), (n, k), 'nf4', 64, data, scales, down=v, up=u)
+    _compare(y1[rows.cuda()], expected, 'prefill-sample')
+
+
+def test_quantized_linear_module(rt):
+    import torch_npu_lowbit as lb
+    from torch_npu_lowbit_correction import LowRankCorrection
+    lin = torch.nn.Linear(576, 1536, bias=True)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(1536, 576) * 0.02)
+        lin.bias.copy_(torch.randn(1536) * 0.1)
+    _, u, v = baseline_weight(1536, 576)
+    corr = LowRankCorrection((1536, 576), 32, v.numpy().tobytes(), u.numpy().tobytes())
+    q = lb.QuantizedLinear.from_float(lin, format='int8', correction=corr)
+    assert q.weight.format == 'int8' and q.weight.group_size == 576
+    # the packed bytes equal the reference quantizer's
+    g, data, scales = ref.quantize(lin.weight.detach().numpy(), 'int8')
+    assert q.weight.data == data and q.weight.scales == scales
+    np.testing.assert_array_equal(q.weight.dequantize(), ref.dequantize((1536, 576), 'int8', g, data, scales))
+    x = torch.randn(3, 576).half()
+    expected = ref.linear(x, (1536, 576), 'int8', g, data, scales, down=v, up=u, bias=lin.bias.detach().half())
+    _compare(q(x.cuda()), expected, 'module')
+    with pytest.raises(ValueError):
+        q(x.cuda().float())
+    with pytest.raises(ValueError):
+        q(x.cuda()[:, :100])
+    with pytest.raises(NotImplementedError):
+        lb.QuantizedLinear(q.weight, compact_groups=True)

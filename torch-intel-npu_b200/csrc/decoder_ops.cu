@@ -1,0 +1,360 @@
+// SmolLM decoder ops around the low-bit projections, following the staged fp16
+// rounding of FrozenSmolLayer.reference_cpu (torch_npu_smollm.py:142-193) and
+// FrozenSmolIO (torch_npu_smollm_io.py:45-61).  All HBM-bound, one pass each.
+#include "common.cuh"
+
+namespace lowbit {
+
+__device__ __forceinline__ float block_sum(float v, float *sh) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += sh[i];
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float *sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float t = -INFINITY;
+  for (int i = 0; i < nw; ++i) t = fmaxf(t, sh[i]);
+  return t;
+}
+
+// RMSNorm (torch_npu_smollm.py:166-168), optionally fused with the residual add that
+// precedes it (:184, :192): h = half(x + r) is written back as the new hidden state.
+// One CTA per row; the row is kept in registers (dim <= 8 * 8 * blockDim).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __half *__restrict__ x, const __half *__restrict__ res,
+                                                      __half *__restrict__ res_out, const __half *__restrict__ gamma,
+                                                      __half *__restrict__ out, int dim, float eps) {
+  __shared__ float sh[32];
+  pdl_launch();
+  pdl_wait();
+  const int64_t r = blockIdx.x;
+  const __half *xr = x + r * dim;
+  constexpr int MAXV = 8;  // up to 8 x 8 halves per thread
+  float v[MAXV * 8];
+  float ss = 0.f;
+  const int nvec = dim / 8;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nvec) {
+      uint4 a = *reinterpret_cast<const uint4 *>(xr + c * 8);
+      const __half *ah = reinterpret_cast<const __half *>(&a);
+      if (res) {
+        uint4 b = *reinterpret_cast<const uint4 *>(res + r * dim + c * 8);
+        const __half *bh = reinterpret_cast<const __half *>(&b);
+        uint4 h;
+        __half *hh = reinterpret_cast<__half *>(&h);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hh[j] = __float2half_rn(__half2float(ah[j]) + __half2float(bh[j]));
+        if (res_out) *reinterpret_cast<uint4 *>(res_out + r * dim + c * 8) = h;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i * 8 + j] = __half2float(hh[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i * 8 + j] = __half2float(ah[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[i * 8 + j], v[i * 8 + j], ss);
+    }
+  }
+  const float total = block_sum(ss, sh);
+  const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, float(dim)), eps));
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nvec) {
+      uint4 g = *reinterpret_cast<const uint4 *>(gamma + c * 8);
+      const __half *gh = reinterpret_cast<const __half *>(&g);
+      uint4 o;
+      __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oh[j] = __hmul(__float2half_rn(__fmul_rn(v[i * 8 + j], inv)), gh[j]);
+      *reinterpret_cast<uint4 *>(out + r * dim + c * 8) = o;
+    }
+  }
+}
+
+// RoPE in place (torch_npu_smollm.py:174-177): v = half(half(v*cos) + half(rot(v)*sin)),
+// rot(v) = cat(-v[hd/2:], v[:hd/2]).  One thread per (token, head, i < hd/2) pair.
+__global__ void rope_kernel(__half *__restrict__ q, __half *__restrict__ k, const int32_t *__restrict__ pos,
+                            const __half *__restrict__ cos_t, const __half *__restrict__ sin_t, int tokens, int heads,
+                            int kv_heads, int hd, int q_stride, int k_stride) {
+  pdl_launch();
+  pdl_wait();
+  const int half_d = hd / 2;
+  const int64_t per_tok = int64_t(heads + kv_heads) * half_d;
+  const int64_t total = per_tok * tokens;
+  for (int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; id < total; id += int64_t(gridDim.x) * blockDim.x) {
+    const int t = int(id / per_tok);
+    const int rem = int(id % per_tok);
+    const int h = rem / half_d, i = rem % half_d;
+    __half *base = h < heads ? q + int64_t(t) * q_stride + h * hd : k + int64_t(t) * k_stride + (h - heads) * hd;
+    const int p = pos[t];
+    const __half a = base[i], b = base[i + half_d];
+    const __half c0 = cos_t[int64_t(p) * hd + i], s0 = sin_t[int64_t(p) * hd + i];
+    const __half c1 = cos_t[int64_t(p) * hd + i + half_d], s1 = sin_t[int64_t(p) * hd + i + half_d];
+    base[i] = __hadd(__hmul(a, c0), __hmul(__hneg(b), s0));
+    base[i + half_d] = __hadd(__hmul(b, c1), __hmul(a, s1));
+  }
+}
+
+// KV Select (torch_npu_smollm.py:288-292): cache[b, h, lengths[b], :] = new row.
+__global__ void kv_append_kernel(const __half *__restrict__ k, const __half *__restrict__ v, int kv_stride,
+                                 __half *__restrict__ kc, __half *__restrict__ vc, const int32_t *__restrict__ lengths,
+                                 int batch, int kvh, int hd, int max_pos) {
+  pdl_launch();
+  pdl_wait();
+  const int64_t total = int64_t(batch) * kvh * hd;
+  for (int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; id < total; id += int64_t(gridDim.x) * blockDim.x) {
+    const int b = int(id / (kvh * hd));
+    const int rem = int(id % (kvh * hd));
+    const int h = rem / hd, i = rem % hd;
+    const int p = lengths[b];
+    if (p < 0 || p >= max_pos) continue;
+    const int64_t dst = ((int64_t(b) * kvh + h) * max_pos + p) * hd + i;
+    kc[dst] = k[int64_t(b) * kv_stride + h * hd + i];
+    vc[dst] = v[int64_t(b) * kv_stride + h * hd + i];
+  }
+}
+
+// One-token GQA attention with the reference staging (torch_npu_smollm.py:178-182):
+// s_j = half(half(q.k_j) * scale); p = half(softmax_f32(s)); out = half(sum_j p_j v_j).
+// One CTA per (batch, kv head) serving the `rep` query heads that share it.
+template <int HD>
+__global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__restrict__ q, int q_stride,
+                                                               const __half *__restrict__ kc,
+                                                               const __half *__restrict__ vc,
+                                                               const int32_t *__restrict__ lengths,
+                                                               __half *__restrict__ out, int heads, int kvh,
+                                                               int max_pos, float scale) {
+  extern __shared__ float sc[];  // [rep][len]
+  __shared__ float sh[32];
+  __shared__ float outp[8][8][HD];  // [warp][rep][dim] partials (rep <= 8)
+  pdl_launch();
+  pdl_wait();
+  const int b = blockIdx.x / kvh, g = blockIdx.x % kvh;
+  const int rep = heads / kvh;
+  const int len = min(lengths[b] + 1, max_pos);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const __half *kbase = kc + (int64_t(b) * kvh + g) * max_pos * HD;
+  const __half *vbase = vc + (int64_t(b) * kvh + g) * max_pos * HD;
+  // scores: 8 lanes per key row (16 bytes each), 4 keys per warp per step
+  const int sub = lane >> 3, l8 = lane & 7;
+  float qv[8][8];
+  for (int r = 0; r < rep; ++r) {
+    const __half *qr = q + int64_t(b) * q_stride + (g * rep + r) * HD + l8 * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qv[r][j] = __half2float(qr[j]);
+  }
+  for (int j0 = warp * 4; j0 < len; j0 += nw * 4) {
+    const int j = j0 + sub;
+    float d[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) d[r] = 0.f;
+    if (j < len) {
+      const uint4 kv = *reinterpret_cast<const uint4 *>(kbase + int64_t(j) * HD + l8 * 8);
+      const __half *kh = reinterpret_cast<const __half *>(&kv);
+      for (int r = 0; r < rep; ++r)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d[r] = fmaf(qv[r][e], __half2float(kh[e]), d[r]);
+    }
+    for (int r = 0; r < rep; ++r) {
+      float s = d[r];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      if (l8 == 0 && j < len) sc[r * max_pos + j] = __half2float(__float2half_rn(__half2float(__float2half_rn(s)) * scale));
+    }
+  }
+  __syncthreads();
+  for (int r = 0; r < rep; ++r) {
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < len; j += blockDim.x) mx = fmaxf(mx, sc[r * max_pos + j]);
+    mx = block_max(mx, sh);
+    float sum = 0.f;
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+      const float e = expf(sc[r * max_pos + j] - mx);
+      sc[r * max_pos + j] = e;
+      sum += e;
+    }
+    sum = block_sum(sum, sh);
+    for (int j = threadIdx.x; j < len; j += blockDim.x)
+      sc[r * max_pos + j] = __half2float(__float2half_rn(__fdiv_rn(sc[r * max_pos + j], sum)));
+  }
+  __syncthreads();
+  // out: each warp a strided range of keys, lane covers 2 dims (HD = 64)
+  float acc[8][2];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[r][0] = acc[r][1] = 0.f;
+  for (int j = warp; j < len; j += nw) {
+    const __half2 vv = *reinterpret_cast<const __half2 *>(vbase + int64_t(j) * HD + 2 * lane);
+    const float2 vf = __half22float2(vv);
+    for (int r = 0; r < rep; ++r) {
+      const float pj = sc[r * max_pos + j];
+      acc[r][0] = fmaf(pj, vf.x, acc[r][0]);
+      acc[r][1] = fmaf(pj, vf.y, acc[r][1]);
+    }
+  }
+  for (int r = 0; r < rep; ++r) {
+    outp[warp][r][2 * lane] = acc[r][0];
+    outp[warp][r][2 * lane + 1] = acc[r][1];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rep * HD; i += blockDim.x) {
+    const int r = i / HD, dd = i % HD;
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += outp[w][r][dd];
+    out[int64_t(b) * heads * HD + (g * rep + r) * HD + dd] = __float2half_rn(s);
+  }
+}
+
+// h = half(half(silu(float(gate))) * up)  (torch_npu_smollm.py:189-190)
+__global__ void silu_mul_kernel(const __half *__restrict__ gate, const __half *__restrict__ up, int in_stride,
+                                __half *__restrict__ out, int rows, int cols) {
+  pdl_launch();
+  pdl_wait();
+  const int64_t total = int64_t(rows) * cols;
+  for (int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; id < total; id += int64_t(gridDim.x) * blockDim.x) {
+    const int r = int(id / cols), c = int(id % cols);
+    const float gv = __half2float(gate[int64_t(r) * in_stride + c]);
+    const __half act = __float2half_rn(__fdiv_rn(gv, 1.f + expf(-gv)));
+    out[id] = __hmul(act, up[int64_t(r) * in_stride + c]);
+  }
+}
+
+__global__ void add_kernel(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ out,
+                           int64_t count) {
+  pdl_launch();
+  pdl_wait();
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i]));
+}
+
+// Embedding rows (torch_npu_smollm_io.py:45-50).  Out-of-range ids yield zero rows.
+__global__ void embed_kernel(const int64_t *__restrict__ ids, const __half *__restrict__ table,
+                             __half *__restrict__ out, int64_t tokens, int dim, int64_t vocab) {
+  pdl_launch();
+  pdl_wait();
+  const int64_t total = tokens * dim;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t t = i / dim;
+    const int c = int(i % dim);
+    const int64_t id = ids[t];
+    out[i] = (id >= 0 && id < vocab) ? table[id * dim + c] : __float2half(0.f);
+  }
+}
+
+// Greedy argmax per row, first index on ties (torch.argmax).
+__global__ void __launch_bounds__(1024) argmax_kernel(const __half *__restrict__ logits, int vocab,
+                                                      int64_t *__restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_launch();
+  pdl_wait();
+  const int64_t r = blockIdx.x;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = __half2float(logits[r * vocab + i]);
+    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < int(blockDim.x >> 5); ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+    out[r] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+}  // namespace lowbit
+
+namespace lowbit_host {
+using namespace lowbit;
+
+static unsigned grid_1d(int64_t work, int block) {
+  int64_t g = (work + block - 1) / block;
+  if (g > 148 * 16) g = 148 * 16;
+  return unsigned(g < 1 ? 1 : g);
+}
+
+cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *res, uint16_t *res_out, const uint16_t *gamma,
+                           uint16_t *out, int rows, int dim, float eps, cudaStream_t st) {
+  int threads = 256;
+  while (threads > 32 && (dim / 8) <= threads / 2) threads /= 2;
+  return launch_k(rmsnorm_kernel, dim3(rows), dim3(threads), 0, st, reinterpret_cast<const __half *>(x),
+                  reinterpret_cast<const __half *>(res), reinterpret_cast<__half *>(res_out),
+                  reinterpret_cast<const __half *>(gamma), reinterpret_cast<__half *>(out), dim, eps);
+}
+
+cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint16_t *cos_t, const uint16_t *sin_t,
+                        int tokens, int heads, int kvh, int hd, int q_stride, int k_stride, cudaStream_t st) {
+  const int64_t work = int64_t(tokens) * (heads + kvh) * (hd / 2);
+  return launch_k(rope_kernel, dim3(grid_1d(work, 256)), dim3(256), 0, st, reinterpret_cast<__half *>(q),
+                  reinterpret_cast<__half *>(k), pos, reinterpret_cast<const __half *>(cos_t),
+                  reinterpret_cast<const __half *>(sin_t), tokens, heads, kvh, hd, q_stride, k_stride);
+}
+
+cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *kc, uint16_t *vc,
+                             const int32_t *lengths, int batch, int kvh, int hd, int max_pos, cudaStream_t st) {
+  const int64_t work = int64_t(batch) * kvh * hd;
+  return launch_k(kv_append_kernel, dim3(grid_1d(work, 256)), dim3(256), 0, st, reinterpret_cast<const __half *>(k),
+                  reinterpret_cast<const __half *>(v), kv_stride, reinterpret_cast<__half *>(kc),
+                  reinterpret_cast<__half *>(vc), lengths, batch, kvh, hd, max_pos);
+}
+
+size_t attention_smem(int heads, int kvh, int max_pos) { return size_t(heads / kvh) * max_pos * sizeof(float); }
+
+cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
+                                    const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
+                                    int max_pos, float scale, cudaStream_t st) {
+  if (hd != 64) return cudaErrorInvalidValue;
+  const size_t smem = attention_smem(heads, kvh, max_pos);
+  auto kern = attention_decode_kernel<64>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return launch_k(kern, dim3(batch * kvh), dim3(256), smem, st, reinterpret_cast<const __half *>(q), q_stride,
+                  reinterpret_cast<const __half *>(kc), reinterpret_cast<const __half *>(vc), lengths,
+                  reinterpret_cast<__half *>(out), heads, kvh, max_pos, scale);
+}
+
+cudaError_t launch_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,
+                            cudaStream_t st) {
+  return launch_k(silu_mul_kernel, dim3(grid_1d(int64_t(rows) * cols, 256)), dim3(256), 0, st,
+                  reinterpret_cast<const __half *>(gate), reinterpret_cast<const __half *>(up), in_stride,
+                  reinterpret_cast<__half *>(out), rows, cols);
+}
+
+cudaError_t launch_add(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t count, cudaStream_t st) {
+  return launch_k(add_kernel, dim3(grid_1d(count, 256)), dim3(256), 0, st, reinterpret_cast<const __half *>(a),
+                  reinterpret_cast<const __half *>(b), reinterpret_cast<__half *>(out), count);
+}
+
+cudaError_t launch_embed(const int64_t *ids, const uint16_t *table, uint16_t *out, int64_t tokens, int dim,
+                         int64_t vocab, cudaStream_t st) {
+  return launch_k(embed_kernel, dim3(grid_1d(tokens * dim, 256)), dim3(256), 0, st, ids,
+                  reinterpret_cast<const __half *>(table), reinterpret_cast<__half *>(out), tokens, dim, vocab);
+}
+
+cudaError_t launch_argmax(const uint16_t *logits, int rows, int vocab, int64_t *out, cudaStream_t st) {
+  return launch_k(argmax_kernel, dim3(rows), dim3(1024), 0, st, reinterpret_cast<const __half *>(logits), vocab, out);
+}
+
+}  // namespace lowbit_host

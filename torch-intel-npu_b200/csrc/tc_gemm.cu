@@ -1,0 +1,571 @@
+// K3: dequant-GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Orientation ("weights as A"): one CTA owns 128 weight rows (the MMA M dimension) and
+// BM activation rows (the MMA N dimension, 16..256).  Per 64-wide K stage:
+//   * warp 0 (one lane) TMA-loads the packed code tile [128 rows x 32|64 bytes] and the
+//     activation tile [BM x 64] fp16 (128-byte swizzle) -- fp16 weights are TMA-loaded
+//     straight into the A buffer;
+//   * warps 2..5 (128 threads, one weight row each) dequantize the codes exactly as the
+//     reference does (rn16(code * scale)) into the K-major 128B-swizzled A buffer;
+//   * warp 1 (one lane) issues 4 x tcgen05.mma (M=128, N=BM, K=16, fp16 in, fp32 TMEM
+//     accumulate) and commits to the stage's "empty" barrier.
+// The rank-32 correction is a second TMEM accumulator: U tile [128 x 32] and z tile
+// [BM x 32] (64-byte swizzle) feed two more MMAs, so delta = z.U^T lands beside y_q.
+// Epilogue (warps 2..5): tcgen05.ld, per-row INT8 scale, y = half(half(acc)+bias),
+// y = half(y + half(delta)), stored transposed to y[m, n].
+// Split-K (small M): each split writes fp32 partials to the caller's workspace and
+// finalize_kernel applies the same epilogue.
+// No TMA multicast is used anywhere.  Every mbarrier wait is bounded: on timeout the
+// kernel records LB_ERR_TIMEOUT in the workspace flag, drains and returns.
+#include <cuda.h>
+#include "common.cuh"
+
+namespace lowbit {
+
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false if the CTA aborted or the wait timed out.
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(a, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(a, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) { *abort_flag = 1; return false; }
+  }
+  return true;
+}
+
+// Time-bounded wait that ignores the abort flag (used to drain copies in flight).
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t a, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(a, parity))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int c0, int c1, uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(mbar)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major, swizzled (bits: start>>4 [0,14), LBO>>4 [16,30),
+// SBO>>4 [32,46), version 1 at [46,48), layout type at [61,64)).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = uint64_t((saddr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(sbo_bytes >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(layout) << 61;
+  return d;
+}
+constexpr uint32_t kSwizzle128 = 2, kSwizzle64 = 4;
+
+// instruction descriptor, kind::f16: D f32, A/B f16, both K-major, N>>3 at 17, M>>4 at 24
+__host__ __device__ constexpr uint32_t umma_idesc(int m, int n) {
+  return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int FMT> struct TcFmt;
+template <> struct TcFmt<LB_FMT_INT4> { static constexpr int CODE_BYTES = 32; };
+template <> struct TcFmt<LB_FMT_NF4> { static constexpr int CODE_BYTES = 32; };
+template <> struct TcFmt<LB_FMT_INT8> { static constexpr int CODE_BYTES = 64; };
+template <> struct TcFmt<LB_FMT_FP16> { static constexpr int CODE_BYTES = 0; };
+
+template <int BM> struct TcStages { static constexpr int S = BM >= 256 ? 3 : (BM >= 128 ? 4 : 6); };
+
+template <int FMT, int BM> struct TcLayout {
+  static constexpr int S = TcStages<BM>::S;
+  static constexpr int A_BYTES = 128 * 128;          // 128 rows x 64 fp16
+  static constexpr int B_BYTES = BM * 128;           // BM rows x 64 fp16
+  static constexpr int C_BYTES = 128 * TcFmt<FMT>::CODE_BYTES;
+  static constexpr int A2_BYTES = 128 * 64;          // U tile, 32 fp16 per row
+  static constexpr int B2_BYTES = BM * 64;           // z tile
+  static constexpr int LUT_BYTES = FMT == LB_FMT_NF4 ? 256 * 32 * 4 : 0;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + S * A_BYTES;
+  static constexpr int OFF_A2 = OFF_B + S * B_BYTES;
+  static constexpr int OFF_B2 = OFF_A2 + A2_BYTES;
+  static constexpr int OFF_C = ((OFF_B2 + B2_BYTES + 1023) / 1024) * 1024;
+  static constexpr int OFF_LUT = OFF_C + S * C_BYTES;
+  static constexpr int OFF_BAR = ((OFF_LUT + LUT_BYTES + 15) / 16) * 16;
+  static constexpr int BAR_BYTES = (3 * S + 2) * 8 + 16;
+  static constexpr int TOTAL = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
+};
+
+struct TcParams {
+  int m, n, k, group;
+  int stages_total;   // k / 64
+  int stages_per_split;
+  int splits;
+  int has_corr;
+  int ldy;            // output row stride (elements)
+  const __half *scales;
+  const __half *bias;
+  __half *y;
+  float *partial;     // [splits, m, n] when splits > 1
+  int *err;           // workspace error flag
+};
+
+__device__ __forceinline__ uint32_t swz128(int row, int chunk) {
+  return uint32_t((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+template <int FMT, int BM>
+__global__ void __launch_bounds__(192, 1)
+    tc_linear_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_z,
+                     const TcParams p) {
+  using L = TcLayout<FMT, BM>;
+  constexpr int S = L::S;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+  // bars: full_tma[S], full_a[S], empty[S], corr_full, acc_full
+  const uint32_t bar_full_tma = smem_u32(bars), bar_full_a = smem_u32(bars + S), bar_empty = smem_u32(bars + 2 * S);
+  const uint32_t bar_corr = smem_u32(bars + 3 * S), bar_acc = smem_u32(bars + 3 * S + 1);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * 128, m0 = blockIdx.y * BM;
+  const int split = blockIdx.z;
+  const int st_begin = split * p.stages_per_split;
+  const int st_end = min(p.stages_total, st_begin + p.stages_per_split);
+  const int nst = st_end - st_begin;
+  const bool corr = p.has_corr && p.splits == 1;
+  constexpr bool kDequant = FMT != LB_FMT_FP16;
+  constexpr uint32_t kCols = BM * 2 <= 32 ? 32 : (BM * 2 <= 64 ? 64 : (BM * 2 <= 128 ? 128 : (BM * 2 <= 256 ? 256 : 512)));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(bar_full_tma + 8 * s, 1);
+      mbar_init(bar_full_a + 8 * s, 4);   // one arrive per dequant warp
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_corr, 1);
+    mbar_init(bar_acc, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (FMT == LB_FMT_NF4) {
+    uint32_t *lut = reinterpret_cast<uint32_t *>(smem + L::OFF_LUT);
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+      const int e = i >> 5;
+      lut[i] = h2_as_u32(__halves2half2(__float2half_rn(nf4_value(e & 15)), __float2half_rn(nf4_value(e >> 4))));
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  pdl_launch();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_acc = tmem, tmem_corr = tmem + BM;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      pdl_wait();
+      if (corr) {
+        mbar_expect_tx(bar_corr, L::A2_BYTES + L::B2_BYTES);
+        tma_load_2d(sbase + L::OFF_A2, &tm_u, 0, n0, bar_corr);
+        tma_load_2d(sbase + L::OFF_B2, &tm_z, 0, m0, bar_corr);
+      }
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) break;
+        const int kst = st_begin + i;
+        ++issued;
+        mbar_expect_tx(bar_full_tma + 8 * s, (kDequant ? L::C_BYTES : L::A_BYTES) + L::B_BYTES);
+        if (kDequant)
+          tma_load_2d(sbase + L::OFF_C + s * L::C_BYTES, &tm_w, kst * TcFmt<FMT>::CODE_BYTES, n0, bar_full_tma + 8 * s);
+        else
+          tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &tm_w, kst * 64, n0, bar_full_tma + 8 * s);
+        tma_load_2d(sbase + L::OFF_B + s * L::B_BYTES, &tm_x, kst * 64, m0, bar_full_tma + 8 * s);
+      }
+      if (*abort_flag) {
+        // let every copy this thread started land before the CTA can exit
+        for (int j = issued > S ? issued - S : 0; j < issued; ++j) mbar_wait_drain(bar_full_tma + 8 * (j % S), (j / S) & 1);
+        if (corr) mbar_wait_drain(bar_corr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(128, BM);
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        if (!mbar_wait(bar_full_tma + 8 * s, ph, abort_flag)) break;
+        if (kDequant && !mbar_wait(bar_full_a + 8 * s, ph, abort_flag)) break;
+        tc_fence_after();
+        const uint64_t ad = umma_desc(sbase + L::OFF_A + s * L::A_BYTES, 1024, kSwizzle128);
+        const uint64_t bd = umma_desc(sbase + L::OFF_B + s * L::B_BYTES, 1024, kSwizzle128);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tmem_acc, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(bar_empty + 8 * s);
+      }
+      if (corr && !*abort_flag && mbar_wait(bar_corr, 0, abort_flag)) {
+        tc_fence_after();
+        const uint64_t ad = umma_desc(sbase + L::OFF_A2, 512, kSwizzle64);
+        const uint64_t bd = umma_desc(sbase + L::OFF_B2, 512, kSwizzle64);
+        umma_f16(tmem_corr, ad, bd, idesc, 0u);
+        umma_f16(tmem_corr, ad + 2, bd + 2, idesc, 1u);
+      }
+      umma_commit(bar_acc);  // fires when every MMA issued above has completed
+    }
+  } else {
+    // --------------------- dequant (mainloop) + epilogue ----------------------
+    const int t = threadIdx.x - 64;      // 0..127: weight row within the tile
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane this warp may access
+    if (kDequant) {
+      const int n = n0 + t;
+      const bool nok = n < p.n;
+      const int gpr = p.k / p.group;
+      const bool per_row = FMT == LB_FMT_INT8 && p.group == p.k;
+      const uint32_t *lut = reinterpret_cast<const uint32_t *>(smem + L::OFF_LUT) + lane;
+      auto load_scales = [&](int kst, __half2 &sa, __half2 &sb) {
+        if (per_row || !nok) { sa = sb = __float2half2_rn(1.f); return; }
+        const int g0 = (kst * 64) / p.group, g1 = (kst * 64 + 32) / p.group;
+        const __half a = p.scales[int64_t(n) * gpr + g0], b = p.scales[int64_t(n) * gpr + g1];
+        sa = __halves2half2(a, a);
+        sb = __halves2half2(b, b);
+      };
+      __half2 sa, sb, na, nb;
+      pdl_wait();
+      if (nst > 0) load_scales(st_begin, na, nb);
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        sa = na; sb = nb;
+        if (i + 1 < nst) load_scales(st_begin + i + 1, na, nb);
+        if (!mbar_wait(bar_full_tma + 8 * s, ph, abort_flag)) break;
+        const uint8_t *crow = smem + L::OFF_C + s * L::C_BYTES + t * TcFmt<FMT>::CODE_BYTES;
+        uint8_t *abuf = smem + L::OFF_A + s * L::A_BYTES;
+        if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
+          const uint4 c0 = *reinterpret_cast<const uint4 *>(crow);
+          const uint4 c1 = *reinterpret_cast<const uint4 *>(crow + 16);
+          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            uint32_t o[4];
+            if constexpr (FMT == LB_FMT_INT4) {
+              uint32_t q[4];
+              int4_word_to_h2(wv[w], q);   // (e0,e4) (e1,e5) (e2,e6) (e3,e7)
+              o[0] = __byte_perm(q[0], q[1], 0x5410);
+              o[1] = __byte_perm(q[2], q[3], 0x5410);
+              o[2] = __byte_perm(q[0], q[1], 0x7632);
+              o[3] = __byte_perm(q[2], q[3], 0x7632);
+            } else {
+              const uint32_t b = wv[w];
+              o[0] = lut[(b << 5) & 0x1FE0u];
+              o[1] = lut[(b >> 3) & 0x1FE0u];
+              o[2] = lut[(b >> 11) & 0x1FE0u];
+              o[3] = lut[(b >> 19) & 0x1FE0u];
+            }
+            const __half2 sc = w < 4 ? sa : sb;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = h2_as_u32(__hmul2(u32_as_h2(o[j]), sc));
+            *reinterpret_cast<uint4 *>(abuf + swz128(t, w)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        } else {  // INT8: 64 bytes -> 8 chunks of 8 halves
+          uint32_t wv[16];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * v);
+            wv[4 * v] = c.x; wv[4 * v + 1] = c.y; wv[4 * v + 2] = c.z; wv[4 * v + 3] = c.w;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t a[2], b[2], o[4];
+            int8_word_to_h2(wv[2 * j], a);       // (e0,e2) (e1,e3)
+            int8_word_to_h2(wv[2 * j + 1], b);   // (e4,e6) (e5,e7)
+            o[0] = __byte_perm(a[0], a[1], 0x5410);
+            o[1] = __byte_perm(a[0], a[1], 0x7632);
+            o[2] = __byte_perm(b[0], b[1], 0x5410);
+            o[3] = __byte_perm(b[0], b[1], 0x7632);
+            if (!per_row) {
+              const __half2 sc = j < 4 ? sa : sb;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) o[q] = h2_as_u32(__hmul2(u32_as_h2(o[q]), sc));
+            }
+            *reinterpret_cast<uint4 *>(abuf + swz128(t, j)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_full_a + 8 * s);
+      }
+    } else {
+      pdl_wait();
+    }
+
+    // ------------------------------- epilogue ---------------------------------
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_acc, 0, abort_flag));
+    tc_fence_after();
+    if (ok) {
+      const int n = n0 + row;
+      float rs = 1.f;
+      if (FMT == LB_FMT_INT8 && p.group == p.k && n < p.n) rs = __half2float(p.scales[n]);
+      const float bias = (p.bias && n < p.n) ? __half2float(p.bias[n]) : 0.f;
+      const uint32_t lane_off = uint32_t(32 * (warp & 3)) << 16;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BM; c0 += 16) {
+        uint32_t a[16], d[16];
+        tmem_ld16(tmem_acc + lane_off + c0, a);
+        if (corr) tmem_ld16(tmem_corr + lane_off + c0, d);
+        tmem_ld_wait();
+        if (n < p.n) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m >= p.m) break;
+            float v = __uint_as_float(a[j]) * rs;
+            if (p.splits > 1) {
+              p.partial[(int64_t(split) * p.m + m) * p.n + n] = v;
+              continue;
+            }
+            __half yq = __float2half_rn(v);
+            if (p.bias) yq = __float2half_rn(__half2float(yq) + bias);
+            if (corr) yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(__uint_as_float(d[j]))));
+            p.y[int64_t(m) * p.ldy + n] = yq;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) atomicExch(p.err, LB_ERR_TIMEOUT);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+  }
+}
+
+// Sum split-K partials and apply the reference epilogue.  One thread per (m, n).
+__global__ void tc_finalize_kernel(int m, int n, int splits, const float *__restrict__ partial,
+                                   const __half *__restrict__ bias, const __half *__restrict__ z,
+                                   const __half *__restrict__ up, int rank, __half *__restrict__ y, int ldy) {
+  pdl_launch();
+  pdl_wait();
+  const int64_t total = int64_t(m) * n;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < splits; ++s) v += partial[int64_t(s) * total + i];
+    const int mm = int(i / n), nn = int(i % n);
+    __half yq = __float2half_rn(v);
+    if (bias) yq = __float2half_rn(__half2float(yq) + __half2float(bias[nn]));
+    if (z) {
+      float d = 0.f;
+      for (int r = 0; r < rank; ++r) d = fmaf(__half2float(z[mm * 32 + r]), __half2float(up[int64_t(nn) * rank + r]), d);
+      yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(d)));
+    }
+    y[int64_t(mm) * ldy + nn] = yq;
+  }
+}
+
+}  // namespace lowbit
+
+// ------------------------------------ host ------------------------------------------
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace lowbit_host {
+using namespace lowbit;
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D tensor map: inner extent `inner` elements, `outer` rows, row pitch `pitch` bytes.
+static bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+                     uint64_t pitch, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_supported(int fmt, int group, int m, int n, int k, int rank) {
+  if (m < 1 || n < 1 || k < 64 || k % 64) return false;
+  if (fmt == LB_FMT_INT4 || fmt == LB_FMT_NF4 || (fmt == LB_FMT_INT8 && group != k))
+    if (group % 32) return false;
+  if (rank > 0 && (rank > 32 || rank % 8)) return false;
+  return true;
+}
+
+int tc_block_m(int m) {
+  if (m <= 16) return 16;
+  if (m <= 32) return 32;
+  if (m <= 64) return 64;
+  if (m <= 128) return 128;
+  return 256;
+}
+
+int tc_splits(int m, int n, int k) {
+  const int bm = tc_block_m(m);
+  const int tiles = ((n + 127) / 128) * ((m + bm - 1) / bm);
+  const int stages = k / 64;
+  int s = 1;
+  while (tiles * s * 2 <= 2 * 148 && stages / (s * 2) >= 4) s *= 2;
+  return s;
+}
+
+size_t tc_partial_bytes(int m, int n, int k) {
+  const int s = tc_splits(m, n, k);
+  return s > 1 ? size_t(s) * m * n * sizeof(float) : 0;
+}
+
+template <int FMT, int BM>
+static cudaError_t launch_tc_t(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &u, const CUtensorMap &z,
+                               const TcParams &p, cudaStream_t st) {
+  using L = TcLayout<FMT, BM>;
+  auto kern = tc_linear_kernel<FMT, BM>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.n + 127) / 128, (p.m + BM - 1) / BM, p.splits);
+  return launch_k(kern, grid, dim3(192), size_t(L::TOTAL), st, w, x, u, z, p);
+}
+
+template <int FMT>
+static cudaError_t launch_tc_f(int bm, const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &u,
+                               const CUtensorMap &z, const TcParams &p, cudaStream_t st) {
+  switch (bm) {
+    case 16: return launch_tc_t<FMT, 16>(w, x, u, z, p, st);
+    case 32: return launch_tc_t<FMT, 32>(w, x, u, z, p, st);
+    case 64: return launch_tc_t<FMT, 64>(w, x, u, z, p, st);
+    case 128: return launch_tc_t<FMT, 128>(w, x, u, z, p, st);
+    default: return launch_tc_t<FMT, 256>(w, x, u, z, p, st);
+  }
+}
+
+// y = x . W^T with the reference epilogue.  z (if non-null) is [m, 32] fp16 in device
+// memory, up is U [n, rank].  partial: fp32 scratch of tc_partial_bytes(); err: int flag.
+cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                      const uint16_t *scales, const uint16_t *z, int ldz_unused, const uint16_t *up, int rank,
+                      const uint16_t *bias, uint16_t *y, int ldy, float *partial, int *err, cudaStream_t st) {
+  (void)ldz_unused;
+  const int bm = tc_block_m(m);
+  int splits = tc_splits(m, n, k);
+  {
+    const int per = (k / 64 + splits - 1) / splits;
+    splits = (k / 64 + per - 1) / per;
+  }
+  CUtensorMap tw, tx, tu, tz;
+  bool ok;
+  if (fmt == LB_FMT_FP16)
+    ok = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, codes, k, n, uint64_t(k) * 2, 64, 128,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+  else {
+    const uint64_t rb = fmt == LB_FMT_INT8 ? uint64_t(k) : uint64_t(k) / 2;
+    ok = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, rb, n, rb, fmt == LB_FMT_INT8 ? 64 : 32, 128,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  ok = ok && make_map(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m, uint64_t(k) * 2, 64, bm, CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool corr = z != nullptr && splits == 1;
+  if (corr) {
+    ok = ok && make_map(&tu, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, up, rank, n, uint64_t(rank) * 2, 32, 128,
+                        CU_TENSOR_MAP_SWIZZLE_64B);
+    ok = ok && make_map(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, z, 32, m, 64, 32, bm, CU_TENSOR_MAP_SWIZZLE_64B);
+  } else {
+    tu = tx;
+    tz = tx;
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  TcParams p = {};
+  p.m = m; p.n = n; p.k = k; p.group = fmt == LB_FMT_FP16 ? k : group;
+  p.stages_total = k / 64;
+  p.stages_per_split = (p.stages_total + splits - 1) / splits;
+  p.splits = (p.stages_total + p.stages_per_split - 1) / p.stages_per_split;  // no empty split
+  p.has_corr = corr ? 1 : 0;
+  p.ldy = ldy;
+  p.scales = reinterpret_cast<const __half *>(scales);
+  p.bias = reinterpret_cast<const __half *>(bias);
+  p.y = reinterpret_cast<__half *>(y);
+  p.partial = partial;
+  p.err = err;
+  cudaError_t e;
+  switch (fmt) {
+    case LB_FMT_INT4: e = launch_tc_f<LB_FMT_INT4>(bm, tw, tx, tu, tz, p, st); break;
+    case LB_FMT_NF4: e = launch_tc_f<LB_FMT_NF4>(bm, tw, tx, tu, tz, p, st); break;
+    case LB_FMT_INT8: e = launch_tc_f<LB_FMT_INT8>(bm, tw, tx, tu, tz, p, st); break;
+    default: e = launch_tc_f<LB_FMT_FP16>(bm, tw, tx, tu, tz, p, st); break;
+  }
+  if (e != cudaSuccess || p.splits == 1) return e;
+  const int64_t total = int64_t(m) * n;
+  int blocks = int((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  return launch_k(tc_finalize_kernel, dim3(blocks), dim3(256), 0, st, m, n, p.splits, (const float *)partial,
+                  reinterpret_cast<const __half *>(bias), reinterpret_cast<const __half *>(z),
+                  reinterpret_cast<const __half *>(up), rank, reinterpret_cast<__half *>(y), ldy);
+}
+
+}  // namespace lowbit_host
