@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/lowbit.h"
+#include "lowbit.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "liblowbit is built for sm_100a (B200) only"
@@ -24,6 +24,28 @@ __host__ __device__ constexpr float nf4_value(int i) {
 
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Runtime-indexed copy of the codebook in constant memory (a runtime index into the
+// constexpr table above would be lowered to a per-thread stack array).
+static __constant__ float c_nf4[16] = {
+    -1.f, -.6961928009986877f, -.5250730514526367f, -.39491748809814453f, -.28444138169288635f,
+    -.18477343022823334f, -.09105003625154495f, 0.f, .07958029955625534f, .16093020141124725f,
+    .24611230194568634f, .33791524171829224f, .44070982933044434f, .5626170039176941f, .7229568362236023f, 1.f};
+
+// Fill the per-lane-replicated byte->half2 NF4 table used by the decode and GEMM
+// kernels: word (e * 32 + l) = (NF4h[e & 15], NF4h[e >> 4]) for every lane l.  Each
+// thread writes whole 128-byte entries with 16-byte stores rotated by lane, so the
+// stores of a warp hit distinct bank groups.
+__device__ __forceinline__ void fill_nf4_pair_lut(uint32_t *lut) {
+  const int lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < 256; e += blockDim.x) {
+    const __half2 v = __halves2half2(__float2half_rn(c_nf4[e & 15]), __float2half_rn(c_nf4[e >> 4]));
+    const uint32_t u = h2_as_u32(v);
+    const uint4 q = make_uint4(u, u, u, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) reinterpret_cast<uint4 *>(lut + e * 32)[(j + lane) & 7] = q;
+  }
+}
 
 // acc += a.lo * b.lo + a.hi * b.hi with exact fp16 products, fp32 accumulation
 // (mixed-precision fma of PTX ISA 8.6, one instruction per product).

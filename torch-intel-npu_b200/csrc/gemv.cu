@@ -48,8 +48,60 @@ template <int MT> struct Unroll { static constexpr int U = MT == 1 ? 8 : 4; };
 // x pairs held by one lane for one activation row: 16 half2 (4-bit), 8 (int8), 4 (fp16)
 template <int FMT> struct XRegs { static constexpr int N = FmtTraits<FMT>::E / 2; };
 
+// Dot-product formulation (compile-time): 0 = mixed-precision fma (f16 x f16 -> f32),
+// 1 = convert to fp32 + fmaf, 2 = fp16x2 fma into a per-chunk half2 partial,
+// 3 = convert to fp32 + packed fp32x2 fma.  x pairs are stored in the matching type.
+#ifndef LOWBIT_GEMV_DOT
+#define LOWBIT_GEMV_DOT 3
+#endif
+constexpr int kDot = LOWBIT_GEMV_DOT;
+constexpr bool kXFloat = kDot == 1 || kDot == 3;
+struct XPair { uint32_t h; float2 f; };
+
+__device__ __forceinline__ XPair make_xpair(uint32_t h2) {
+  XPair x;
+  if constexpr (kXFloat) x.f = __half22float2(u32_as_h2(h2)); else x.h = h2;
+  return x;
+}
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long A = (unsigned long long)__float_as_uint(a.x) | ((unsigned long long)__float_as_uint(a.y) << 32);
+  unsigned long long B = (unsigned long long)__float_as_uint(b.x) | ((unsigned long long)__float_as_uint(b.y) << 32);
+  unsigned long long C = (unsigned long long)__float_as_uint(c.x) | ((unsigned long long)__float_as_uint(c.y) << 32);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(C) : "l"(A), "l"(B));
+  return make_float2(__uint_as_float(uint32_t(C)), __uint_as_float(uint32_t(C >> 32)));
+}
+
+// per-chunk partial sum of 2 * pairs products
+struct Part {
+  float f; __half2 h; float2 f2;
+  __device__ __forceinline__ void init() {
+    if constexpr (kDot == 2) h = __float2half2_rn(0.f);
+    else if constexpr (kDot == 3) f2 = make_float2(0.f, 0.f);
+    else f = 0.f;
+  }
+  __device__ __forceinline__ void fma(uint32_t w2, const XPair &x) {
+    if constexpr (kDot == 0) {
+      fma2_f16_f32(f, w2, x.h);
+    } else if constexpr (kDot == 1) {
+      const float2 wf = __half22float2(u32_as_h2(w2));
+      f = fmaf(wf.x, x.f.x, f);
+      f = fmaf(wf.y, x.f.y, f);
+    } else if constexpr (kDot == 2) {
+      h = __hfma2(u32_as_h2(w2), u32_as_h2(x.h), h);
+    } else {
+      f2 = ffma2(__half22float2(u32_as_h2(w2)), x.f, f2);
+    }
+  }
+  __device__ __forceinline__ float sum() const {
+    if constexpr (kDot == 2) return __low2float(h) + __high2float(h);
+    else if constexpr (kDot == 3) return f2.x + f2.y;
+    else return f;
+  }
+};
+
 template <int FMT>
-__device__ __forceinline__ void load_x_chunk(const __half *xrow, int chunk, bool valid, uint32_t (&xr)[XRegs<FMT>::N]) {
+__device__ __forceinline__ void load_x_chunk(const __half *xrow, int chunk, bool valid, XPair (&xr)[XRegs<FMT>::N]) {
   constexpr int E = FmtTraits<FMT>::E;
   constexpr int V = E / 8;  // uint4 loads
   uint32_t nat[E / 2];
@@ -63,34 +115,34 @@ __device__ __forceinline__ void load_x_chunk(const __half *xrow, int chunk, bool
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t A = nat[w * 4 + 0], B = nat[w * 4 + 1], C = nat[w * 4 + 2], D = nat[w * 4 + 3];
-      xr[w * 4 + 0] = __byte_perm(A, C, 0x5410);
-      xr[w * 4 + 1] = __byte_perm(A, C, 0x7632);
-      xr[w * 4 + 2] = __byte_perm(B, D, 0x5410);
-      xr[w * 4 + 3] = __byte_perm(B, D, 0x7632);
+      xr[w * 4 + 0] = make_xpair(__byte_perm(A, C, 0x5410));
+      xr[w * 4 + 1] = make_xpair(__byte_perm(A, C, 0x7632));
+      xr[w * 4 + 2] = make_xpair(__byte_perm(B, D, 0x5410));
+      xr[w * 4 + 3] = make_xpair(__byte_perm(B, D, 0x7632));
     }
   } else if constexpr (FMT == LB_FMT_INT8) {
     // pairs (x0,x2),(x1,x3) per group of 4, matching int8_word_to_h2
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t A = nat[w * 2 + 0], B = nat[w * 2 + 1];
-      xr[w * 2 + 0] = __byte_perm(A, B, 0x5410);
-      xr[w * 2 + 1] = __byte_perm(A, B, 0x7632);
+      xr[w * 2 + 0] = make_xpair(__byte_perm(A, B, 0x5410));
+      xr[w * 2 + 1] = make_xpair(__byte_perm(A, B, 0x7632));
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < E / 2; ++i) xr[i] = nat[i];
+    for (int i = 0; i < E / 2; ++i) xr[i] = make_xpair(nat[i]);
   }
 }
 
 // dot of one 16-byte weight chunk with the lane's x pairs for MT activation rows
 template <int FMT, int MT, bool EXACT>
 __device__ __forceinline__ void chunk_dot(const uint4 &q, __half2 s2, const uint32_t *lut_lane,
-                                          const uint32_t (&xr)[MT][XRegs<FMT>::N], float (&acc)[MT]) {
+                                          const XPair (&xr)[MT][XRegs<FMT>::N], float (&acc)[MT]) {
   const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-  if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
-    float part[MT];
+  Part part[MT];
 #pragma unroll
-    for (int mm = 0; mm < MT; ++mm) part[mm] = 0.f;
+  for (int mm = 0; mm < MT; ++mm) part[mm].init();
+  if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       uint32_t p[4];
@@ -107,39 +159,38 @@ __device__ __forceinline__ void chunk_dot(const uint4 &q, __half2 s2, const uint
       for (int j = 0; j < 4; ++j) {
         if constexpr (EXACT) p[j] = h2_as_u32(__hmul2(u32_as_h2(p[j]), s2));  // rn16(code * scale)
 #pragma unroll
-        for (int mm = 0; mm < MT; ++mm) {
-          if constexpr (EXACT) fma2_f16_f32(acc[mm], p[j], xr[mm][w * 4 + j]);
-          else fma2_f16_f32(part[mm], p[j], xr[mm][w * 4 + j]);
-        }
+        for (int mm = 0; mm < MT; ++mm) part[mm].fma(p[j], xr[mm][w * 4 + j]);
       }
     }
-    if constexpr (!EXACT) {
+    if constexpr (EXACT) {
+#pragma unroll
+      for (int mm = 0; mm < MT; ++mm) acc[mm] += part[mm].sum();
+    } else {
       const float s = __low2float(s2);
 #pragma unroll
-      for (int mm = 0; mm < MT; ++mm) acc[mm] = fmaf(part[mm], s, acc[mm]);
+      for (int mm = 0; mm < MT; ++mm) acc[mm] = fmaf(part[mm].sum(), s, acc[mm]);
     }
   } else if constexpr (FMT == LB_FMT_INT8) {
-    float part[MT];
-#pragma unroll
-    for (int mm = 0; mm < MT; ++mm) part[mm] = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       uint32_t p[2];
       int8_word_to_h2(wv[w], p);
 #pragma unroll
       for (int mm = 0; mm < MT; ++mm) {
-        fma2_f16_f32(part[mm], p[0], xr[mm][w * 2 + 0]);
-        fma2_f16_f32(part[mm], p[1], xr[mm][w * 2 + 1]);
+        part[mm].fma(p[0], xr[mm][w * 2 + 0]);
+        part[mm].fma(p[1], xr[mm][w * 2 + 1]);
       }
     }
     const float s = __low2float(s2);  // codes are exact; the group scale factors out
 #pragma unroll
-    for (int mm = 0; mm < MT; ++mm) acc[mm] = fmaf(part[mm], s, acc[mm]);
+    for (int mm = 0; mm < MT; ++mm) acc[mm] = fmaf(part[mm].sum(), s, acc[mm]);
   } else {
 #pragma unroll
     for (int w = 0; w < 4; ++w)
 #pragma unroll
-      for (int mm = 0; mm < MT; ++mm) fma2_f16_f32(acc[mm], wv[w], xr[mm][w]);
+      for (int mm = 0; mm < MT; ++mm) part[mm].fma(wv[w], xr[mm][w]);
+#pragma unroll
+    for (int mm = 0; mm < MT; ++mm) acc[mm] += part[mm].sum();
   }
 }
 
@@ -170,12 +221,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       prefetch_l2_bulk(base + off, uint32_t(total - off < 65536 ? total - off : 65536));
   }
   if constexpr (FMT == LB_FMT_NF4) {
-    // lut[e * 32 + l] = (NF4h[e & 15], NF4h[e >> 4]) for every lane l
-    for (int i = threadIdx.x; i < kLutWords; i += blockDim.x) {
-      const int e = i >> 5;
-      const __half2 v = __halves2half2(__float2half_rn(nf4_value(e & 15)), __float2half_rn(nf4_value(e >> 4)));
-      lut[i] = h2_as_u32(v);
-    }
+    fill_nf4_pair_lut(lut);
     __syncthreads();
   }
   pdl_wait();
@@ -193,7 +239,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   for (int s = wk; s < p.nslices; s += p.warps_k) {
     const int chunk = s * p.slice_width + lane;
     const bool active = lane < p.slice_width && chunk < chunks;
-    uint32_t xr[MT][XN];
+    XPair xr[MT][XN];
 #pragma unroll
     for (int mm = 0; mm < MT; ++mm) load_x_chunk<FMT>(p.x + size_t(mm) * p.k, chunk, active && mm < p.m, xr[mm]);
     const int gidx = active ? (chunk * E) / p.group : 0;
@@ -315,7 +361,7 @@ __global__ void linear_generic_kernel(int fmt, int m, int n, int k, int group, c
     } else {
       const uint32_t b = codes[e >> 1];
       const uint32_t c = (e & 1) ? (b >> 4) : (b & 15u);
-      const __half v = fmt == LB_FMT_INT4 ? __int2half_rn(int(c ^ 8u) - 8) : __float2half_rn(nf4_value(int(c)));
+      const __half v = fmt == LB_FMT_INT4 ? __int2half_rn(int(c ^ 8u) - 8) : __float2half_rn(c_nf4[c]);
       w = __half2float(__hmul(v, scales[e / group]));
     }
     acc = fmaf(__half2float(x[int64_t(mm) * k + kk]), w, acc);

@@ -90,7 +90,7 @@ __device__ __forceinline__ __half code_value(int fmt, const uint8_t *codes, int6
   const uint32_t b = codes[e >> 1];
   const uint32_t c = (e & 1) ? (b >> 4) : (b & 15u);
   if (fmt == LB_FMT_INT4) return __int2half_rn(int((c ^ 8u)) - 8);
-  return __float2half_rn(nf4_value(int(c)));
+  return __float2half_rn(c_nf4[c]);
 }
 
 __global__ void dequantize_kernel(int fmt, const uint8_t *__restrict__ codes, const __half *__restrict__ scales,

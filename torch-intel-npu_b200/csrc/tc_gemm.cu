@@ -178,7 +178,8 @@ __global__ void __launch_bounds__(192, 1)
   const int st_begin = split * p.stages_per_split;
   const int st_end = min(p.stages_total, st_begin + p.stages_per_split);
   const int nst = st_end - st_begin;
-  const bool corr = p.has_corr && p.splits == 1;
+  // the correction accumulator is computed once per output tile: by split 0
+  const bool corr = p.has_corr && split == 0;
   constexpr bool kDequant = FMT != LB_FMT_FP16;
   constexpr uint32_t kCols = BM * 2 <= 32 ? 32 : (BM * 2 <= 64 ? 64 : (BM * 2 <= 128 ? 128 : (BM * 2 <= 256 ? 256 : 512)));
 
@@ -193,13 +194,7 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (FMT == LB_FMT_NF4) {
-    uint32_t *lut = reinterpret_cast<uint32_t *>(smem + L::OFF_LUT);
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-      const int e = i >> 5;
-      lut[i] = h2_as_u32(__halves2half2(__float2half_rn(nf4_value(e & 15)), __float2half_rn(nf4_value(e >> 4))));
-    }
-  }
+  if (FMT == LB_FMT_NF4) fill_nf4_pair_lut(reinterpret_cast<uint32_t *>(smem + L::OFF_LUT));
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kCols));
@@ -376,6 +371,7 @@ __global__ void __launch_bounds__(192, 1)
             float v = __uint_as_float(a[j]) * rs;
             if (p.splits > 1) {
               p.partial[(int64_t(split) * p.m + m) * p.n + n] = v;
+              if (corr) p.partial[(int64_t(p.splits) * p.m + m) * p.n + n] = __uint_as_float(d[j]);
               continue;
             }
             __half yq = __float2half_rn(v);
@@ -397,25 +393,29 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// Sum split-K partials and apply the reference epilogue.  One thread per (m, n).
-__global__ void tc_finalize_kernel(int m, int n, int splits, const float *__restrict__ partial,
-                                   const __half *__restrict__ bias, const __half *__restrict__ z,
-                                   const __half *__restrict__ up, int rank, __half *__restrict__ y, int ldy) {
+// Sum split-K partials and apply the reference epilogue.  When has_corr, slice
+// [splits] of the partial buffer holds the fp32 correction accumulator z . U^T.
+// One thread per 4 consecutive outputs of a row.
+__global__ void tc_finalize_kernel(int m, int n, int splits, int has_corr, const float *__restrict__ partial,
+                                   const __half *__restrict__ bias, __half *__restrict__ y, int ldy) {
   pdl_launch();
   pdl_wait();
   const int64_t total = int64_t(m) * n;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-    float v = 0.f;
-    for (int s = 0; s < splits; ++s) v += partial[int64_t(s) * total + i];
-    const int mm = int(i / n), nn = int(i % n);
-    __half yq = __float2half_rn(v);
-    if (bias) yq = __float2half_rn(__half2float(yq) + __half2float(bias[nn]));
-    if (z) {
-      float d = 0.f;
-      for (int r = 0; r < rank; ++r) d = fmaf(__half2float(z[mm * 32 + r]), __half2float(up[int64_t(nn) * rank + r]), d);
-      yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(d)));
+  const int nq = (n + 3) / 4;
+  for (int64_t q = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; q < int64_t(m) * nq; q += int64_t(gridDim.x) * blockDim.x) {
+    const int mm = int(q / nq), n0 = int(q % nq) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int nn = n0 + j;
+      if (nn >= n) break;
+      const int64_t i = int64_t(mm) * n + nn;
+      float v = 0.f;
+      for (int s = 0; s < splits; ++s) v += partial[int64_t(s) * total + i];
+      __half yq = __float2half_rn(v);
+      if (bias) yq = __float2half_rn(__half2float(yq) + __half2float(bias[nn]));
+      if (has_corr) yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(partial[int64_t(splits) * total + i])));
+      y[int64_t(mm) * ldy + nn] = yq;
     }
-    y[int64_t(mm) * ldy + nn] = yq;
   }
 }
 
@@ -481,9 +481,8 @@ int tc_splits(int m, int n, int k) {
 
 size_t tc_partial_bytes(int m, int n, int k) {
   const int s = tc_splits(m, n, k);
-  return s > 1 ? size_t(s) * m * n * sizeof(float) : 0;
+  return s > 1 ? size_t(s + 1) * m * n * sizeof(float) : 0;  // + one slice for the correction
 }
-
 template <int FMT, int BM>
 static cudaError_t launch_tc_t(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &u, const CUtensorMap &z,
                                const TcParams &p, cudaStream_t st) {
@@ -530,7 +529,7 @@ cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x
                   CU_TENSOR_MAP_SWIZZLE_NONE);
   }
   ok = ok && make_map(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m, uint64_t(k) * 2, 64, bm, CU_TENSOR_MAP_SWIZZLE_128B);
-  const bool corr = z != nullptr && splits == 1;
+  const bool corr = z != nullptr;
   if (corr) {
     ok = ok && make_map(&tu, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, up, rank, n, uint64_t(rank) * 2, 32, 128,
                         CU_TENSOR_MAP_SWIZZLE_64B);
@@ -560,12 +559,11 @@ cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x
     default: e = launch_tc_f<LB_FMT_FP16>(bm, tw, tx, tu, tz, p, st); break;
   }
   if (e != cudaSuccess || p.splits == 1) return e;
-  const int64_t total = int64_t(m) * n;
+  const int64_t total = int64_t(m) * ((n + 3) / 4);
   int blocks = int((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  return launch_k(tc_finalize_kernel, dim3(blocks), dim3(256), 0, st, m, n, p.splits, (const float *)partial,
-                  reinterpret_cast<const __half *>(bias), reinterpret_cast<const __half *>(z),
-                  reinterpret_cast<const __half *>(up), rank, reinterpret_cast<__half *>(y), ldy);
+  return launch_k(tc_finalize_kernel, dim3(blocks), dim3(256), 0, st, m, n, p.splits, p.has_corr, (const float *)partial,
+                  reinterpret_cast<const __half *>(bias), reinterpret_cast<__half *>(y), ldy);
 }
 
 }  // namespace lowbit_host

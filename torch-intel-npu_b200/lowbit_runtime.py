@@ -81,6 +81,14 @@ def require_cuda():
     return lib()
 
 
+def cuda_device(device=None):
+    """Normalise a device spec to an indexed CUDA device (``cuda`` -> ``cuda:<current>``)."""
+    dev = torch.device('cuda') if device is None else torch.device(device)
+    if dev.type != 'cuda':
+        raise ValueError('The B200 low-bit path runs on CUDA devices only')
+    return torch.device('cuda', torch.cuda.current_device() if dev.index is None else dev.index)
+
+
 def check(status, what):
     if status == OK:
         return

@@ -88,7 +88,7 @@ class PackedWeight:
     def to_device(self, device=None):
         """Upload codes and scales once: (codes uint8, scales fp16) CUDA tensors."""
         rt.require_cuda()
-        dev = torch.device('cuda') if device is None else torch.device(device)
+        dev = rt.cuda_device(device)
         codes = torch.frombuffer(bytearray(self.data), dtype=torch.uint8).to(dev)
         scales = torch.frombuffer(bytearray(self.scales), dtype=torch.float16).to(dev)
         return codes, scales
@@ -154,7 +154,7 @@ class QuantizedLinear(torch.nn.Module):
         self._compact_groups = False
         self._activation_scale = None
         rt.require_cuda()
-        self._device = torch.device('cuda') if device is None else torch.device(device)
+        self._device = rt.cuda_device(device)
         self._codes, self._scales = weight.to_device(self._device)
         if bias is not None:
             if (not isinstance(bias, torch.Tensor) or bias.device.type != 'cpu' or bias.shape != (weight.shape[0],)
