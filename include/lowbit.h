@@ -4,7 +4,9 @@
  * Plain pointers, sizes and a CUDA stream passed as `void*`.  Every entry point
  * returns an lb_status and never aborts.  All device buffers belong to the caller;
  * the library allocates no device memory (scratch is a caller-provided workspace
- * sized by the matching *_workspace_bytes query).  Outputs must not alias inputs.
+ * sized by the matching *_workspace_bytes query, 16-byte aligned and zero-filled once
+ * before its first use -- kernels that keep arrival counters there leave them at zero
+ * again).  A workspace serves one stream at a time.  Outputs must not alias inputs.
  * Work is stream-ordered and asynchronous unless a comment says otherwise.
  *
  * Packed formats are the reference's canonical bytes (torch_npu_lowbit.py):

@@ -72,7 +72,8 @@ def test_path_selection():
     import lowbit_runtime as rt
     assert rt.linear_select('nf4', 64, 1, 8192, 2048) == 'gemv'
     assert rt.linear_select('int4', 128, 4, 2048, 8192) == 'gemv'
-    assert rt.linear_select('nf4', 64, 16, 8192, 2048) == 'tc'
+    assert rt.linear_select('nf4', 64, 16, 8192, 2048) == 'gemv'
+    assert rt.linear_select('nf4', 64, 17, 8192, 2048) == 'tc'
     assert rt.linear_select('int8', 576, 128, 1536, 576) == 'tc'
     assert rt.linear_select('int4', 3, 1, 5, 9) == 'generic'      # odd shapes / groups
     assert rt.linear_select('nf4', 64, 128, 8192, 2048, 32) == 'tc'
@@ -84,8 +85,8 @@ def test_workspace_query_covers_correction_and_split_k():
     small = rt.linear_workspace_bytes('nf4', 64, 1, 8192, 2048, 0)
     corr = rt.linear_workspace_bytes('nf4', 64, 1, 8192, 2048, 32)
     assert small >= 256 and corr >= small + 64
-    split = rt.linear_workspace_bytes('nf4', 64, 16, 2048, 8192, 32)
-    assert split >= 16 * 2048 * 4
+    split = rt.linear_workspace_bytes('nf4', 64, 32, 2048, 8192, 32)
+    assert split >= 32 * 2048 * 4
 
 
 def test_host_fault_injection(lib):

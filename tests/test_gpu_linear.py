@@ -166,6 +166,25 @@ def test_ragged_shapes_and_ranks(rt, n, k, fmt, g, rank):
         _compare(y, expected, (n, k, fmt, g, rank, m))
 
 
+@pytest.mark.parametrize('plan', ['1,1,1', '2,4,1', '8,2,1', '8,1,4', '4,2,2', '1,4,8'])
+@pytest.mark.parametrize('fmt,g,m', [('nf4', 64, 1), ('int4', 128, 5), ('int8', 2048, 16), ('int8', 64, 3)])
+def test_gemv_work_splits_agree(rt, monkeypatch, plan, fmt, g, m):
+    """Every GEMV work split (warps over K, rows per warp, cross-CTA K splits with the
+    workspace reduction) gives the same parity; cross-CTA splits are deterministic."""
+    monkeypatch.setenv('LOWBIT_GEMV_PLAN', plan)
+    n, k = 2048, 2048
+    w, u, v = baseline_weight(n, k, seed=21)
+    group, data, scales = ref.quantize(w.numpy(), fmt, g)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(22)).half()
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    expected = _oracle(x, (n, k), fmt, group, data, scales, down=v, up=u)
+    y1 = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda(), path='gemv')
+    y2 = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda(), path='gemv')
+    _compare(y1, expected, (plan, fmt, g, m))
+    assert torch.equal(y1, y2)
+
+
 def test_large_prefill_shape_properties(rt):
     """Full BASELINE prefill size: deterministic, zero-in gives the correction-free zero,
     and a row sample matches the oracle."""

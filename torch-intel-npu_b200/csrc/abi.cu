@@ -21,7 +21,8 @@ cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, co
                                    cudaStream_t st);
 cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
                         const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
-                        uint16_t *y, cudaStream_t st);
+                        uint16_t *y, void *scratch, int *counters, cudaStream_t st);
+size_t gemv_workspace_bytes(int fmt, int m, int n, int k);
 cudaError_t launch_linear_generic(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
                                   const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank,
                                   const uint16_t *bias, uint16_t *y, cudaStream_t st);
@@ -104,7 +105,11 @@ size_t code_bytes(int fmt, int64_t n, int64_t k) {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-constexpr size_t kHeader = 256;  // error flag + padding
+// Workspace header: [0, 256) status word; [256, 256 + 16 KiB) GEMV arrival counters.
+// Both sit at fixed offsets, so whatever shape a call has, the counters it relies on
+// are the ones the previous call left at zero.
+constexpr size_t kCounterOffset = 256;
+constexpr size_t kHeader = 256 + 4096 * sizeof(int);
 
 int select_path(int fmt, int group, int m, int n, int k, int rank) {
   if (gemv_supported(fmt, group, m, n, k)) return LB_PATH_GEMV;
@@ -117,9 +122,10 @@ size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * 32 * 2)
 // z projection for the TC path at larger M runs on the tensor cores too
 bool z_on_tc(int m, int k, int rank) { return m > 16 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0); }
 
-size_t linear_ws(int path, int m, int n, int k, int rank) {
+size_t linear_ws(int path, int fmt, int group, int m, int n, int k, int rank) {
   size_t b = kHeader + z_bytes(m, rank);
-  if (path == LB_PATH_TC) {
+  if (path == LB_PATH_GEMV && gemv_supported(fmt, group, m, n, k)) b += align256(gemv_workspace_bytes(fmt, m, n, k));
+  if (path == LB_PATH_TC && tc_supported(fmt, group, m, n, k, rank)) {
     b += align256(tc_partial_bytes(m, n, k));
     if (rank > 0 && z_on_tc(m, k, rank)) b += align256(tc_partial_bytes(m, rank, k));
   }
@@ -215,10 +221,9 @@ size_t lb_linear_workspace_bytes(int fmt, int group, int m, int n, int k, int ra
   const int g = fmt == LB_FMT_FP16 ? k : group;
   size_t best = 0;
   for (int path = LB_PATH_GEMV; path <= LB_PATH_GENERIC; ++path) {
-    const size_t b = linear_ws(path, m, n, k, rank);
+    const size_t b = linear_ws(path, fmt, g, m, n, k, rank);
     if (b > best) best = b;
   }
-  (void)g;
   return best;
 }
 
@@ -242,7 +247,7 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
     if (auto_path == LB_PATH_TC) path = LB_PATH_GENERIC; else return LB_ERR_UNSUPPORTED;
   }
   if (path != LB_PATH_GEMV && path != LB_PATH_TC && path != LB_PATH_GENERIC) return LB_ERR_INVALID_ARGUMENT;
-  const size_t need = linear_ws(path, m, n, k, rank);
+  const size_t need = linear_ws(path, fmt, group, m, n, k, rank);
   if (!workspace || workspace_bytes < need) return LB_ERR_WORKSPACE;
   const size_t yb = size_t(m) * n * 2;
   if (overlaps(y, yb, x, size_t(m) * k * 2) || overlaps(y, yb, codes, code_bytes(fmt, n, k)) ||
@@ -270,7 +275,10 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
     if (e != cudaSuccess) return cuda_status(e);
   }
   switch (path) {
-    case LB_PATH_GEMV: e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, st); break;
+    case LB_PATH_GEMV:
+      e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, rest,
+                      reinterpret_cast<int *>(ws + kCounterOffset), st);
+      break;
     case LB_PATH_TC:
       e = launch_tc(fmt, group, m, n, k, x, codes, scales, z, 32, up, rank, bias, y, n,
                     reinterpret_cast<float *>(rest), err, st);

@@ -1,37 +1,30 @@
-// K2: decode dequant-GEMV for small M (x rows held in registers), with the rank-r
-// correction applied in the epilogue.  HBM-bound by design:
-//  * each lane streams 16-byte packed chunks of a weight row (128-bit coalesced loads,
-//    L1 no-allocate), a warp covers up to 32 chunks of one row = one "K slice";
-//  * the lane's slice of x (M rows) is loaded once and reused for every weight row;
-//  * INT4 codes are unpacked in registers with lop3 + one exact fp16 op per pair,
-//    NF4 codes through a per-lane-replicated 256-entry (byte -> half2) table in shared
-//    memory (conflict-free), INT8 with byte_perm + one exact fp16 subtract;
-//  * 4-bit weights are dequantized exactly as the reference does, rn16(code * scale),
-//    and multiplied with x in fp32 (mixed-precision fma, exact products);
-//  * partial sums are reduced with warp shuffles and across K slices in shared memory;
-//  * epilogue: y = half(half(acc) [+ bias]) then half(y + half(z . U[n]^T)).
-// Reference semantics: torch_npu_lowbit.py:67-75 (dequant), torch_npu_smollm.py:150-164.
+// K2: decode dequant-GEMV for M <= 16 with the rank-r correction in the epilogue.
+//
+// HBM-bound by design.  Each warp streams 16-row weight groups: lane (g, t) = (lane/4,
+// lane%4) issues one 128-bit coalesced load of row g and one of row g+8 per 64-byte
+// K block (4 lanes cover a row's 64 contiguous bytes), dequantizes its 32 (4-bit),
+// 16 (INT8) or 8 (fp16) elements in registers -- INT4 with lop3 + one exact fp16 op
+// per pair, NF4 through a per-lane-replicated 256-entry byte->half2 table in shared
+// memory (conflict free), INT8 with byte_perm + one exact fp16 subtract -- and
+// multiplies them by the group scale exactly as the reference dequantizes
+// (rn16(code * scale), torch_npu_lowbit.py:67-75).  The dequantized registers are
+// used directly as the A operand of mma.sync m16n8k16 (fp16 x fp16 products,
+// fp32 accumulation); x is the B operand, one activation row per column, so every
+// M <= 8 costs the same as M = 1 and the dot product costs no FMA-pipe work.
+// The K order inside an MMA is a permutation: each lane's x pairs are loaded once per
+// K block in the same order the unpack produces the weight pairs, so no weight
+// relayout is needed -- the canonical reference bytes are streamed as they are.
+// Partial sums are reduced across the CTA's K-split warps in shared memory and, when
+// the K range is split across CTAs, through fp32 partials in the caller's workspace:
+// the last CTA of a row set (atomic counter, self-resetting) sums them in a fixed
+// order, so results are deterministic.  Epilogue (torch_npu_smollm.py:150-164):
+// y = half(acc) (per-row INT8 scale first), half(y + bias), half(y + half(z . U[n]^T)).
+#include <cstdio>
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace lowbit {
-
-struct GemvParams {
-  int m, n, k, group;
-  const __half *x;       // [m, k]
-  const uint8_t *codes;  // packed rows
-  const __half *scales;  // [n, k/group] (unused for FP16)
-  const __half *z;       // [m, 32] correction projection half(x . V^T), or null
-  const __half *up;      // [n, rank]
-  int rank;
-  const __half *bias;    // [n] or null
-  __half *y;             // [m, n]
-  int nslices;           // K slices
-  int slice_width;       // chunks per slice (<= 32)
-  int warps_k;           // warps along K in a CTA (<= nslices)
-  int rows_per_warp;     // rows handled by each warp (multiple of the unroll)
-  int row_groups;        // warps along N in a CTA
-  int prefetch;          // issue an L2 bulk prefetch of the CTA's weight slab first
-};
 
 template <int FMT> struct FmtTraits;
 template <> struct FmtTraits<LB_FMT_INT4> { static constexpr int E = 32; static constexpr int BITS = 4; };
@@ -39,186 +32,150 @@ template <> struct FmtTraits<LB_FMT_NF4> { static constexpr int E = 32; static c
 template <> struct FmtTraits<LB_FMT_INT8> { static constexpr int E = 16; static constexpr int BITS = 8; };
 template <> struct FmtTraits<LB_FMT_FP16> { static constexpr int E = 8; static constexpr int BITS = 16; };
 
-constexpr int kMaxWarps = 8;
-constexpr int kMaxRowsCta = 64;
+constexpr int kWarps = 8;
+constexpr int kMaxRowGroups = 2;          // 16-row groups per warp
 constexpr int kLutWords = 256 * 32;
+constexpr int kMaxGemvCounters = 4096;    // arrival counters available in the workspace
 
-template <int MT> struct Unroll { static constexpr int U = MT == 1 ? 8 : 4; };
-
-// x pairs held by one lane for one activation row: 16 half2 (4-bit), 8 (int8), 4 (fp16)
-template <int FMT> struct XRegs { static constexpr int N = FmtTraits<FMT>::E / 2; };
-
-// Dot-product formulation (compile-time): 0 = mixed-precision fma (f16 x f16 -> f32),
-// 1 = convert to fp32 + fmaf, 2 = fp16x2 fma into a per-chunk half2 partial,
-// 3 = convert to fp32 + packed fp32x2 fma.  x pairs are stored in the matching type.
-#ifndef LOWBIT_GEMV_DOT
-#define LOWBIT_GEMV_DOT 3
-#endif
-constexpr int kDot = LOWBIT_GEMV_DOT;
-constexpr bool kXFloat = kDot == 1 || kDot == 3;
-struct XPair { uint32_t h; float2 f; };
-
-__device__ __forceinline__ XPair make_xpair(uint32_t h2) {
-  XPair x;
-  if constexpr (kXFloat) x.f = __half22float2(u32_as_h2(h2)); else x.h = h2;
-  return x;
-}
-
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  unsigned long long A = (unsigned long long)__float_as_uint(a.x) | ((unsigned long long)__float_as_uint(a.y) << 32);
-  unsigned long long B = (unsigned long long)__float_as_uint(b.x) | ((unsigned long long)__float_as_uint(b.y) << 32);
-  unsigned long long C = (unsigned long long)__float_as_uint(c.x) | ((unsigned long long)__float_as_uint(c.y) << 32);
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(C) : "l"(A), "l"(B));
-  return make_float2(__uint_as_float(uint32_t(C)), __uint_as_float(uint32_t(C >> 32)));
-}
-
-// per-chunk partial sum of 2 * pairs products
-struct Part {
-  float f; __half2 h; float2 f2;
-  __device__ __forceinline__ void init() {
-    if constexpr (kDot == 2) h = __float2half2_rn(0.f);
-    else if constexpr (kDot == 3) f2 = make_float2(0.f, 0.f);
-    else f = 0.f;
-  }
-  __device__ __forceinline__ void fma(uint32_t w2, const XPair &x) {
-    if constexpr (kDot == 0) {
-      fma2_f16_f32(f, w2, x.h);
-    } else if constexpr (kDot == 1) {
-      const float2 wf = __half22float2(u32_as_h2(w2));
-      f = fmaf(wf.x, x.f.x, f);
-      f = fmaf(wf.y, x.f.y, f);
-    } else if constexpr (kDot == 2) {
-      h = __hfma2(u32_as_h2(w2), u32_as_h2(x.h), h);
-    } else {
-      f2 = ffma2(__half22float2(u32_as_h2(w2)), x.f, f2);
-    }
-  }
-  __device__ __forceinline__ float sum() const {
-    if constexpr (kDot == 2) return __low2float(h) + __high2float(h);
-    else if constexpr (kDot == 3) return f2.x + f2.y;
-    else return f;
-  }
+struct GemvParams {
+  int m, n, k, group;
+  const __half *x;       // [m, k]
+  const uint8_t *codes;  // packed rows, canonical reference layout
+  const __half *scales;  // [n, k/group] (unused for FP16)
+  const __half *z;       // [m, 32] correction projection half(x . V^T), or null
+  const __half *up;      // [n, rank]
+  int rank;
+  const __half *bias;    // [n] or null
+  __half *y;             // [m, n]
+  int warps_k;           // warps splitting a CTA's K range (1, 2, 4, 8)
+  int rpw;               // 16-row groups per warp (<= kMaxRowGroups)
+  int kblocks;           // 64-byte K blocks per row
+  int kb_per_split;      // K blocks per CTA (gridDim.y splits)
+  float *partial;        // [splits, m, n] fp32 when gridDim.y > 1
+  int *counters;         // [gridDim.x] arrival counters (zero between calls)
+  int prefetch;
 };
 
-template <int FMT>
-__device__ __forceinline__ void load_x_chunk(const __half *xrow, int chunk, bool valid, XPair (&xr)[XRegs<FMT>::N]) {
-  constexpr int E = FmtTraits<FMT>::E;
-  constexpr int V = E / 8;  // uint4 loads
-  uint32_t nat[E / 2];
-#pragma unroll
-  for (int v = 0; v < V; ++v) {
-    uint4 q = valid ? *reinterpret_cast<const uint4 *>(xrow + size_t(chunk) * E + v * 8) : make_uint4(0, 0, 0, 0);
-    nat[v * 4 + 0] = q.x; nat[v * 4 + 1] = q.y; nat[v * 4 + 2] = q.z; nat[v * 4 + 3] = q.w;
-  }
-  if constexpr (FMT == LB_FMT_INT4) {
-    // pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7) per group of 8, matching int4_word_to_h2
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t A = nat[w * 4 + 0], B = nat[w * 4 + 1], C = nat[w * 4 + 2], D = nat[w * 4 + 3];
-      xr[w * 4 + 0] = make_xpair(__byte_perm(A, C, 0x5410));
-      xr[w * 4 + 1] = make_xpair(__byte_perm(A, C, 0x7632));
-      xr[w * 4 + 2] = make_xpair(__byte_perm(B, D, 0x5410));
-      xr[w * 4 + 3] = make_xpair(__byte_perm(B, D, 0x7632));
-    }
-  } else if constexpr (FMT == LB_FMT_INT8) {
-    // pairs (x0,x2),(x1,x3) per group of 4, matching int8_word_to_h2
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t A = nat[w * 2 + 0], B = nat[w * 2 + 1];
-      xr[w * 2 + 0] = make_xpair(__byte_perm(A, B, 0x5410));
-      xr[w * 2 + 1] = make_xpair(__byte_perm(A, B, 0x7632));
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < E / 2; ++i) xr[i] = make_xpair(nat[i]);
-  }
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// dot of one 16-byte weight chunk with the lane's x pairs for MT activation rows
-template <int FMT, int MT, bool EXACT>
-__device__ __forceinline__ void chunk_dot(const uint4 &q, __half2 s2, const uint32_t *lut_lane,
-                                          const XPair (&xr)[MT][XRegs<FMT>::N], float (&acc)[MT]) {
+// The lane's 16-byte chunk -> its fp16 pairs, in the format's natural unpack order.
+//   INT4: word w -> (e0,e4) (e1,e5) (e2,e6) (e3,e7) of elements 8w..8w+7
+//   NF4 : byte b of word w -> (e2b, e2b+1)
+//   INT8: word w -> (e0,e2) (e1,e3) of elements 4w..4w+3
+//   FP16: natural pairs
+template <int FMT>
+__device__ __forceinline__ void unpack_chunk(const uint4 &q, __half2 s2, bool scale, const uint32_t *lut_lane,
+                                             uint32_t (&p)[FmtTraits<FMT>::E / 2]) {
   const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-  Part part[MT];
-#pragma unroll
-  for (int mm = 0; mm < MT; ++mm) part[mm].init();
   if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      uint32_t p[4];
       if constexpr (FMT == LB_FMT_INT4) {
-        int4_word_to_h2(wv[w], p);
+        uint32_t o[4];
+        int4_word_to_h2(wv[w], o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[4 * w + j] = o[j];
       } else {
         const uint32_t b = wv[w];
-        p[0] = lut_lane[((b << 5) & 0x1FE0u)];        // byte0 * 32 words
-        p[1] = lut_lane[((b >> 3) & 0x1FE0u)];        // byte1
-        p[2] = lut_lane[((b >> 11) & 0x1FE0u)];       // byte2
-        p[3] = lut_lane[((b >> 19) & 0x1FE0u)];       // byte3
+        p[4 * w + 0] = lut_lane[(b << 5) & 0x1FE0u];
+        p[4 * w + 1] = lut_lane[(b >> 3) & 0x1FE0u];
+        p[4 * w + 2] = lut_lane[(b >> 11) & 0x1FE0u];
+        p[4 * w + 3] = lut_lane[(b >> 19) & 0x1FE0u];
       }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if constexpr (EXACT) p[j] = h2_as_u32(__hmul2(u32_as_h2(p[j]), s2));  // rn16(code * scale)
-#pragma unroll
-        for (int mm = 0; mm < MT; ++mm) part[mm].fma(p[j], xr[mm][w * 4 + j]);
-      }
-    }
-    if constexpr (EXACT) {
-#pragma unroll
-      for (int mm = 0; mm < MT; ++mm) acc[mm] += part[mm].sum();
-    } else {
-      const float s = __low2float(s2);
-#pragma unroll
-      for (int mm = 0; mm < MT; ++mm) acc[mm] = fmaf(part[mm].sum(), s, acc[mm]);
     }
   } else if constexpr (FMT == LB_FMT_INT8) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      uint32_t p[2];
-      int8_word_to_h2(wv[w], p);
-#pragma unroll
-      for (int mm = 0; mm < MT; ++mm) {
-        part[mm].fma(p[0], xr[mm][w * 2 + 0]);
-        part[mm].fma(p[1], xr[mm][w * 2 + 1]);
-      }
+      uint32_t o[2];
+      int8_word_to_h2(wv[w], o);
+      p[2 * w] = o[0];
+      p[2 * w + 1] = o[1];
     }
-    const float s = __low2float(s2);  // codes are exact; the group scale factors out
-#pragma unroll
-    for (int mm = 0; mm < MT; ++mm) acc[mm] = fmaf(part[mm].sum(), s, acc[mm]);
   } else {
 #pragma unroll
-    for (int w = 0; w < 4; ++w)
+    for (int w = 0; w < 4; ++w) p[w] = wv[w];
+  }
+  if (scale) {
 #pragma unroll
-      for (int mm = 0; mm < MT; ++mm) part[mm].fma(wv[w], xr[mm][w]);
-#pragma unroll
-    for (int mm = 0; mm < MT; ++mm) acc[mm] += part[mm].sum();
+    for (int i = 0; i < FmtTraits<FMT>::E / 2; ++i) p[i] = h2_as_u32(__hmul2(u32_as_h2(p[i]), s2));  // rn16(code*scale)
   }
 }
 
-template <int FMT, int MT, bool EXACT>
+// x pairs for the lane's chunk, permuted to match unpack_chunk's pair order.
+template <int FMT>
+__device__ __forceinline__ void load_x_pairs(const __half *xrow, int chunk, bool valid, uint32_t (&xr)[FmtTraits<FMT>::E / 2]) {
+  constexpr int E = FmtTraits<FMT>::E;
+  uint32_t nat[E / 2];
+#pragma unroll
+  for (int v = 0; v < E / 8; ++v) {
+    const uint4 q = valid ? *reinterpret_cast<const uint4 *>(xrow + size_t(chunk) * E + v * 8) : make_uint4(0, 0, 0, 0);
+    nat[v * 4 + 0] = q.x; nat[v * 4 + 1] = q.y; nat[v * 4 + 2] = q.z; nat[v * 4 + 3] = q.w;
+  }
+  if constexpr (FMT == LB_FMT_INT4) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t A = nat[w * 4 + 0], B = nat[w * 4 + 1], C = nat[w * 4 + 2], D = nat[w * 4 + 3];
+      xr[w * 4 + 0] = __byte_perm(A, C, 0x5410);   // (x0, x4)
+      xr[w * 4 + 1] = __byte_perm(A, C, 0x7632);   // (x1, x5)
+      xr[w * 4 + 2] = __byte_perm(B, D, 0x5410);   // (x2, x6)
+      xr[w * 4 + 3] = __byte_perm(B, D, 0x7632);   // (x3, x7)
+    }
+  } else if constexpr (FMT == LB_FMT_INT8) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t A = nat[w * 2 + 0], B = nat[w * 2 + 1];
+      xr[w * 2 + 0] = __byte_perm(A, B, 0x5410);   // (x0, x2)
+      xr[w * 2 + 1] = __byte_perm(A, B, 0x7632);   // (x1, x3)
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < E / 2; ++i) xr[i] = nat[i];
+  }
+}
+
+template <int FMT, int NCOL>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   constexpr int E = FmtTraits<FMT>::E;
-  constexpr int U = Unroll<MT>::U;
-  constexpr int XN = XRegs<FMT>::N;
+  constexpr int NP = E / 2;          // pairs per lane chunk
+  constexpr int TILES = NP / 2;      // m16n8k16 tiles per K block
+  constexpr bool kScaled4 = FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4;
   extern __shared__ __align__(16) uint32_t smem[];
-  float *red = reinterpret_cast<float *>(smem);  // [warps_k][rows_cta][MT]
-  uint32_t *lut = smem + kMaxWarps * kMaxRowsCta * 4;
+  float *red = reinterpret_cast<float *>(smem);                        // [warps_k][rows_cta][16 m]
+  uint32_t *lut = smem + kWarps * 64 * 16;
+  __shared__ int s_last;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wk = warp % p.warps_k, rg = warp / p.warps_k;
-  const int rows_cta = p.row_groups * p.rows_per_warp;
-  const int row_cta0 = blockIdx.x * rows_cta;
+  const int g = lane >> 2, t = lane & 3;
+  const int wr = kWarps / p.warps_k;
+  const int kw = warp % p.warps_k, rw = warp / p.warps_k;
+  const int rows_cta = 16 * wr * p.rpw;
+  const int row0 = blockIdx.x * rows_cta;
+  const int wrow0 = row0 + 16 * p.rpw * rw;   // this warp's first row
   const int64_t row_bytes = int64_t(p.k) * FmtTraits<FMT>::BITS / 8;
   const int chunks = p.k / E;
+  const int kb0 = blockIdx.y * p.kb_per_split;
+  const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
 
   pdl_launch();
   if (p.prefetch && threadIdx.x == 0) {
-    // weights are read-only for the whole program, so they may be requested before
-    // the predecessor kernel finishes
-    const int rows = min(rows_cta, p.n - row_cta0);
-    const uint8_t *base = p.codes + int64_t(row_cta0) * row_bytes;
-    int64_t total = int64_t(rows) * row_bytes;
-    for (int64_t off = 0; off < total; off += 65536)
-      prefetch_l2_bulk(base + off, uint32_t(total - off < 65536 ? total - off : 65536));
+    // weights never change during the program, so their HBM stream may start before
+    // the predecessor kernel has finished
+    const int rows = min(rows_cta, p.n - row0);
+    const int64_t off = int64_t(kb0) * 64;
+    const int64_t end = int64_t(kb1) * 64 < row_bytes ? int64_t(kb1) * 64 : row_bytes;
+    const int64_t len = end - off;
+    if (len == row_bytes) {
+      const uint8_t *base = p.codes + int64_t(row0) * row_bytes;
+      const int64_t total = int64_t(rows) * row_bytes;
+      for (int64_t o = 0; o < total; o += 65536) prefetch_l2_bulk(base + o, uint32_t(total - o < 65536 ? total - o : 65536));
+    } else if ((len & 15) == 0) {
+      for (int r = 0; r < rows; ++r) prefetch_l2_bulk(p.codes + int64_t(row0 + r) * row_bytes + off, uint32_t(len));
+    }
   }
   if constexpr (FMT == LB_FMT_NF4) {
     fill_nf4_pair_lut(lut);
@@ -226,63 +183,120 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   }
   pdl_wait();
 
-  float acc[16][MT];  // rows_per_warp <= 16
-#pragma unroll
-  for (int i = 0; i < 16; ++i)
-#pragma unroll
-    for (int mm = 0; mm < MT; ++mm) acc[i][mm] = 0.f;
-
-  const int groups_per_row = p.k / p.group;
+  const int groups_per_row = FMT == LB_FMT_FP16 ? 1 : p.k / p.group;
+  const bool per_row_scale = FMT == LB_FMT_INT8 && p.group == p.k;
   const uint32_t *lut_lane = lut + lane;
-  const int row_w0 = row_cta0 + rg * p.rows_per_warp;
 
-  for (int s = wk; s < p.nslices; s += p.warps_k) {
-    const int chunk = s * p.slice_width + lane;
-    const bool active = lane < p.slice_width && chunk < chunks;
-    XPair xr[MT][XN];
+  float acc[kMaxRowGroups][NCOL][4];
 #pragma unroll
-    for (int mm = 0; mm < MT; ++mm) load_x_chunk<FMT>(p.x + size_t(mm) * p.k, chunk, active && mm < p.m, xr[mm]);
-    const int gidx = active ? (chunk * E) / p.group : 0;
+  for (int r = 0; r < kMaxRowGroups; ++r)
 #pragma unroll
-    for (int i0 = 0; i0 < 16; i0 += U) {
-      if (i0 >= p.rows_per_warp) break;
-      uint4 q[U];
-      __half2 s2[U];
+    for (int c = 0; c < NCOL; ++c)
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int row = row_w0 + i0 + u;
-        const bool ok = active && row < p.n;
-        q[u] = ok ? ldg_nc_v4(p.codes + int64_t(row) * row_bytes + int64_t(chunk) * 16) : make_uint4(0, 0, 0, 0);
-        if constexpr (FMT != LB_FMT_FP16) {
-          const __half sc = ok ? p.scales[int64_t(row) * groups_per_row + gidx] : __float2half(0.f);
-          s2[u] = __halves2half2(sc, sc);
-        } else {
-          s2[u] = __float2half2_rn(1.f);
+      for (int i = 0; i < 4; ++i) acc[r][c][i] = 0.f;
+
+  // Two K blocks per round: every weight load of the round is in flight before the
+  // first dequant, so each warp pays the memory latency once per round.
+  for (int kbA = kb0 + kw; kbA < kb1; kbA += 2 * p.warps_k) {
+    uint4 q[2][kMaxRowGroups][2];
+    __half2 s2[2][kMaxRowGroups][2];
+    uint32_t xr[2][NCOL][NP];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int kb = kbA + u * p.warps_k;
+      const int chunk = kb * 4 + t;
+      const bool kvalid = kb < kb1 && chunk < chunks;
+#pragma unroll
+      for (int r = 0; r < kMaxRowGroups; ++r) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = wrow0 + 16 * r + g + 8 * h;
+          const bool ok = r < p.rpw && kvalid && row < p.n;
+          q[u][r][h] = ok ? ldg_nc_v4(p.codes + int64_t(row) * row_bytes + int64_t(chunk) * 16) : make_uint4(0, 0, 0, 0);
+          if constexpr (FMT != LB_FMT_FP16) {
+            const __half sc = (ok && !per_row_scale) ? p.scales[int64_t(row) * groups_per_row + (chunk * E) / p.group]
+                                                     : __float2half(1.f);
+            s2[u][r][h] = __halves2half2(sc, sc);
+          } else {
+            s2[u][r][h] = __float2half2_rn(1.f);
+          }
         }
       }
 #pragma unroll
-      for (int u = 0; u < U; ++u) chunk_dot<FMT, MT, EXACT>(q[u], s2[u], lut_lane, xr, acc[i0 + u]);
+      for (int c = 0; c < NCOL; ++c)
+        load_x_pairs<FMT>(p.x + size_t(g + 8 * c) * p.k, chunk, kvalid && g + 8 * c < p.m, xr[u][c]);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (u == 1 && kbA + p.warps_k >= kb1) break;
+#pragma unroll
+      for (int r = 0; r < kMaxRowGroups; ++r) {
+        if (r >= p.rpw) break;
+        uint32_t a0[NP], a1[NP];
+        unpack_chunk<FMT>(q[u][r][0], s2[u][r][0], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lut_lane, a0);
+        unpack_chunk<FMT>(q[u][r][1], s2[u][r][1], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lut_lane, a1);
+#pragma unroll
+        for (int j = 0; j < TILES; ++j) {
+          const uint32_t a[4] = {a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1]};
+#pragma unroll
+          for (int c = 0; c < NCOL; ++c) mma16816(acc[r][c], a, xr[u][c][2 * j], xr[u][c][2 * j + 1]);
+        }
+      }
     }
   }
 
-  // reduce across lanes, then across K slices through shared memory
+  // C fragment: acc[r][c] = {C[g][2t], C[g][2t+1], C[g+8][2t], C[g+8][2t+1]} with rows =
+  // weight rows 16r + {g, g+8}, columns = activation rows 8c + {2t, 2t+1}
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    if (i >= p.rows_per_warp) break;
+  for (int r = 0; r < kMaxRowGroups; ++r) {
+    if (r >= p.rpw) break;
 #pragma unroll
-    for (int mm = 0; mm < MT; ++mm) {
-      const float v = warp_sum(acc[i][mm]);
-      if (lane == 0) red[(wk * rows_cta + rg * p.rows_per_warp + i) * MT + mm] = v;
+    for (int c = 0; c < NCOL; ++c) {
+      float *base = red + (kw * rows_cta + 16 * (p.rpw * rw + r)) * 16 + 8 * c + 2 * t;
+      base[g * 16] = acc[r][c][0];
+      base[g * 16 + 1] = acc[r][c][1];
+      base[(g + 8) * 16] = acc[r][c][2];
+      base[(g + 8) * 16 + 1] = acc[r][c][3];
     }
   }
   __syncthreads();
 
-  for (int idx = threadIdx.x; idx < rows_cta * p.m; idx += blockDim.x) {
-    const int mm = idx / rows_cta, rl = idx % rows_cta;
-    const int n = row_cta0 + rl;
-    if (n >= p.n || mm >= MT) continue;
+  const int splits = gridDim.y;
+  const int outs = rows_cta * p.m;
+  if (splits > 1) {
+    const int64_t mn = int64_t(p.m) * p.n;
+    for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+      const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+      if (n >= p.n) continue;
+      float v = 0.f;
+      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * 16 + mm];
+      p.partial[blockIdx.y * mn + int64_t(mm) * p.n + n] = v;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(p.counters + blockIdx.x, 1) == splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+      const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+      if (n >= p.n) continue;
+      float v = 0.f;
+      for (int sp = 0; sp < splits; ++sp) v += __ldcg(p.partial + sp * mn + int64_t(mm) * p.n + n);
+      red[rl * 16 + mm] = v;   // warp-0 slot reused for the total
+    }
+    if (threadIdx.x == 0) p.counters[blockIdx.x] = 0;   // ready for the next call
+    __syncthreads();
+  }
+
+  for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+    const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+    if (n >= p.n) continue;
     float v = 0.f;
-    for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * MT + mm];
+    if (splits > 1) v = red[rl * 16 + mm];
+    else
+      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * 16 + mm];
+    if (per_row_scale) v *= __half2float(p.scales[n]);
     __half yq = __float2half_rn(v);
     if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
     if (p.z) {
@@ -405,18 +419,10 @@ int gemv_elems(int fmt) { return fmt == LB_FMT_INT8 ? 16 : (fmt == LB_FMT_FP16 ?
 
 bool gemv_supported(int fmt, int group, int m, int n, int k) {
   const int e = gemv_elems(fmt);
-  if (m < 1 || m > 4 || n < 1 || k < e || k % e) return false;
-  if (fmt != LB_FMT_FP16 && (group % e)) return false;
+  if (m < 1 || m > 16 || n < 1 || k < e || k % e) return false;
+  if (fmt != LB_FMT_FP16 && fmt != LB_FMT_INT8 && group % e) return false;
+  if (fmt == LB_FMT_INT8 && group != k && group % e) return false;
   return true;
-}
-
-static bool exact_dequant() {
-  static int v = -1;
-  if (v < 0) {
-    const char *s = getenv("LOWBIT_GEMV_FACTORED_SCALE");
-    v = (s && s[0] == '1') ? 0 : 1;
-  }
-  return v == 1;
 }
 
 static int prefetch_mode() {
@@ -428,26 +434,62 @@ static int prefetch_mode() {
   return v;
 }
 
-template <int FMT, int MT>
-static cudaError_t launch_gemv_t(const GemvParams &p, int ctas, int threads, size_t smem, cudaStream_t st) {
-  cudaError_t e;
-  if (exact_dequant() || FMT == LB_FMT_INT8 || FMT == LB_FMT_FP16) {
-    auto kern = gemv_kernel<FMT, MT, true>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    return launch_k(kern, dim3(ctas), dim3(threads), smem, st, p);
+struct GemvPlan { int warps_k, rpw, splits, kb_per_split, ctas_x; };
+
+// Work split over 16-row groups x 64-byte K blocks.  A rough time model: resident CTAs
+// (2 per SM) must keep ~6 MB of 128-bit loads in flight to cover HBM latency, every
+// extra wave repeats the latency, and a cross-CTA K split adds a reduction pass.
+// LOWBIT_GEMV_PLAN="warps_k,rpw,splits" overrides the choice (tuning).
+static GemvPlan gemv_plan(int fmt, int n, int k) {
+  const int e = gemv_elems(fmt);
+  const int kblocks = (k / e + 3) / 4;
+  const int groups = (n + 15) / 16;
+  if (kblocks < 1 || groups < 1) return {1, 1, 1, 1, 1};
+  int fwk = 0, frpw = 0, fsp = 0;
+  if (const char *env = getenv("LOWBIT_GEMV_PLAN")) sscanf(env, "%d,%d,%d", &fwk, &frpw, &fsp);
+  GemvPlan best = {1, 1, 1, kblocks, groups};
+  double best_cost = 1e30;
+  for (int wk = 1; wk <= kWarps; wk *= 2) {
+    for (int rpw = 1; rpw <= kMaxRowGroups; rpw *= 2) {
+      for (int sp = 1; sp <= 16; sp *= 2) {
+        if (fwk && (wk != fwk || rpw != frpw || sp != fsp)) continue;
+        if (sp > 1 && ((groups + (kWarps / wk) * rpw - 1) / ((kWarps / wk) * rpw)) > kMaxGemvCounters) continue;
+        const int kbs = (kblocks + sp - 1) / sp;
+        if (sp > 1 && kbs < wk) break;
+        if (wk > 1 && kbs < wk) continue;
+        const int wr = kWarps / wk;
+        const int ctas = ((groups + wr * rpw - 1) / (wr * rpw)) * ((kblocks + kbs - 1) / kbs);
+        const int loads = rpw * ((kbs + wk - 1) / wk);          // 1 KB warp loads per warp
+        const int rounds = ((kbs + wk - 1) / wk + 1) / 2;       // two K blocks per round
+        const double resident = ctas < 2 * 148 ? ctas : 2 * 148;
+        const double fill = resident * kWarps * loads * 1024.0 / 6.0e6;
+        const int waves = (ctas + 2 * 148 - 1) / (2 * 148);
+        double cost = waves * (0.6 * rounds + 0.4 + 0.05 * loads) / (fill < 1.0 ? fill : 1.0);
+        if (sp > 1) cost += 0.5;
+        if (cost < best_cost) { best_cost = cost; best = {wk, rpw, (kblocks + kbs - 1) / kbs, kbs, (groups + wr * rpw - 1) / (wr * rpw)}; }
+      }
+    }
   }
-  auto kern = gemv_kernel<FMT, MT, false>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  return best;
+}
+
+size_t gemv_workspace_bytes(int fmt, int m, int n, int k) {
+  const GemvPlan pl = gemv_plan(fmt, n, k);
+  if (pl.splits <= 1) return 0;
+  return size_t(pl.splits) * m * n * sizeof(float);
+}
+
+template <int FMT, int NCOL>
+static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = gemv_kernel<FMT, NCOL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return launch_k(kern, dim3(ctas), dim3(threads), smem, st, p);
+  return launch_k(kern, grid, dim3(32 * kWarps), smem, st, p);
 }
 
 template <int FMT>
-static cudaError_t launch_gemv_f(const GemvParams &p, int mt, int ctas, int threads, size_t smem, cudaStream_t st) {
-  if (mt == 1) return launch_gemv_t<FMT, 1>(p, ctas, threads, smem, st);
-  if (mt == 2) return launch_gemv_t<FMT, 2>(p, ctas, threads, smem, st);
-  return launch_gemv_t<FMT, 4>(p, ctas, threads, smem, st);
+static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_t smem, cudaStream_t st) {
+  return ncol == 1 ? launch_gemv_t<FMT, 1>(p, grid, smem, st) : launch_gemv_t<FMT, 2>(p, grid, smem, st);
 }
 
 cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, const uint16_t *v, uint16_t *z,
@@ -463,11 +505,12 @@ cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, co
                   reinterpret_cast<__half *>(z));
 }
 
-// Choose slices / warps / rows so that the grid covers the SMs with enough 16-byte loads
-// in flight and the K slices of a row stay inside one CTA.
+// scratch: gemv_workspace_bytes() of caller memory for fp32 partials; counters: an int
+// array of kMaxGemvCounters at a fixed place in the workspace, zero before the first call
+// and left at zero by every call.
 cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
                         const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
-                        uint16_t *y, cudaStream_t st) {
+                        uint16_t *y, void *scratch, int *counters, cudaStream_t st) {
   GemvParams p = {};
   p.m = m; p.n = n; p.k = k; p.group = fmt == LB_FMT_FP16 ? k : group;
   p.x = reinterpret_cast<const __half *>(x);
@@ -478,30 +521,25 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   p.rank = rank;
   p.bias = reinterpret_cast<const __half *>(bias);
   p.y = reinterpret_cast<__half *>(y);
-  const int e = gemv_elems(fmt);
-  const int chunks = k / e;
-  p.nslices = (chunks + 31) / 32;
-  p.slice_width = (chunks + p.nslices - 1) / p.nslices;
-  p.warps_k = p.nslices < kMaxWarps ? p.nslices : kMaxWarps;
-  const int mt = m == 1 ? 1 : (m == 2 ? 2 : 4);
-  const int unroll = mt == 1 ? 8 : 4;
-  p.row_groups = kMaxWarps / p.warps_k;
-  // rows per warp: as many as fit while keeping >= ~2 CTAs per SM worth of work
-  int rpw = 16;
-  while (rpw > unroll && int64_t((n + p.row_groups * rpw - 1) / (p.row_groups * rpw)) < 2 * 148) rpw -= unroll;
-  p.rows_per_warp = rpw;
-  while (p.row_groups * p.rows_per_warp > kMaxRowsCta) p.row_groups--;
+  const GemvPlan pl = gemv_plan(fmt, n, k);
+  p.warps_k = pl.warps_k;
+  p.rpw = pl.rpw;
+  p.kblocks = (k / gemv_elems(fmt) + 3) / 4;
+  p.kb_per_split = pl.kb_per_split;
+  if (pl.splits > 1) {
+    p.partial = static_cast<float *>(scratch);
+    p.counters = counters;
+  }
   p.prefetch = prefetch_mode();
-  const int rows_cta = p.row_groups * p.rows_per_warp;
-  const int ctas = (n + rows_cta - 1) / rows_cta;
-  const int threads = 32 * p.warps_k * p.row_groups;
-  size_t smem = size_t(kMaxWarps) * kMaxRowsCta * 4 * sizeof(float);
+  const int ncol = m <= 8 ? 1 : 2;
+  size_t smem = size_t(kWarps) * 64 * 16 * sizeof(float);
   if (fmt == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
+  const dim3 grid(pl.ctas_x, pl.splits);
   switch (fmt) {
-    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, mt, ctas, threads, smem, st);
-    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, mt, ctas, threads, smem, st);
-    case LB_FMT_INT8: return launch_gemv_f<LB_FMT_INT8>(p, mt, ctas, threads, smem, st);
-    default: return launch_gemv_f<LB_FMT_FP16>(p, mt, ctas, threads, smem, st);
+    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st);
+    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st);
+    case LB_FMT_INT8: return launch_gemv_f<LB_FMT_INT8>(p, ncol, grid, smem, st);
+    default: return launch_gemv_f<LB_FMT_FP16>(p, ncol, grid, smem, st);
   }
 }
 
