@@ -114,10 +114,12 @@ int lb_linear_select(int fmt, int group, int m, int n, int k, int rank);
 int lb_rmsnorm(const uint16_t *x, const uint16_t *residual, uint16_t *residual_out,
                const uint16_t *gamma, uint16_t *out, int rows, int dim, float eps, void *stream);
 /* In-place RoPE on q [T, heads, hd] and k [T, kv_heads, hd] with per-token positions:
- * v = half(half(v*cos) + half(rotate_half(v)*sin)) (torch_npu_smollm.py:174-177). */
+ * v = half(half(v*cos) + half(rotate_half(v)*sin)) (torch_npu_smollm.py:174-177).
+ * cos/sin tables are [table_rows, hd]; a token whose position is outside the table is
+ * left unrotated. */
 int lb_rope(uint16_t *q, uint16_t *k, const int32_t *positions, const uint16_t *cos_table,
-            const uint16_t *sin_table, int tokens, int heads, int kv_heads, int head_dim,
-            int q_stride, int k_stride, void *stream);
+            const uint16_t *sin_table, int table_rows, int tokens, int heads, int kv_heads,
+            int head_dim, int q_stride, int k_stride, void *stream);
 /* Append k/v rows [B, kv_heads, hd] into caches [B, kv_heads, max_pos, hd] at position
  * lengths[b] (the KV Select of torch_npu_smollm.py:288-292). */
 int lb_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *k_cache,

@@ -1,0 +1,172 @@
+"""GPU SmolLM decoder vs the CPU oracle (itself pinned bitwise to FrozenSmolLayer.reference_cpu).
+
+Tolerances follow the north star: whole-decoder logits within 0.5% relative L2 of the
+same-format oracle and identical greedy tokens for the first 32 steps; layer outputs
+(prefill attention runs SDPA instead of the reference's fp16-staged softmax) within
+1% relative L2.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import decoder_ref as dref
+from oracle import lowbit_ref as ref
+
+pytestmark = pytest.mark.gpu
+LOGIT_L2 = 5e-3
+LAYER_L2 = 1e-2
+
+
+def rel_l2(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-12))
+
+
+def small_config(layers=2, vocab=1024, hidden=192, heads=3, kv=1, inter=512, theta=10000.0):
+    return dict(model_type='llama', hidden_size=hidden, intermediate_size=inter, num_attention_heads=heads,
+                num_key_value_heads=kv, hidden_act='silu', rms_norm_eps=1e-5, rope_theta=theta, vocab_size=vocab,
+                num_hidden_layers=layers, tie_word_embeddings=True)
+
+
+SMOL135 = dict(small_config(layers=2, vocab=49152, hidden=576, heads=9, kv=3, inter=1536, theta=10000.0))
+
+
+def dims_of(config):
+    return dref.DecoderDims(hidden=config['hidden_size'], intermediate=config['intermediate_size'],
+                            heads=config['num_attention_heads'], kv_heads=config['num_key_value_heads'],
+                            vocab=config['vocab_size'], theta=config['rope_theta'])
+
+
+def corrections_for(shapes, seed):
+    from torch_npu_lowbit_correction import LowRankCorrection
+    gen = torch.Generator().manual_seed(seed)
+    out = {}
+    for name, shape in shapes.items():
+        if len(shape) == 2:
+            n, k = shape
+            down = (torch.randn(32, k, generator=gen) * 1e-3).half()
+            up = (torch.randn(n, 32, generator=gen) * 1e-3).half()
+            out[name] = LowRankCorrection((n, k), 32, down.numpy().tobytes(), up.numpy().tobytes())
+    return out
+
+
+def build(config, mode, group, corrected, seed=0):
+    import torch_npu_lowbit as lb
+    import torch_npu_smollm as sm
+    layers_w, emb, norm = sm.random_smollm_weights(config, seed=seed)
+    fmt = {'w8a16': 'int8', 'w4a16': 'int4', 'nf4a16': 'nf4', 'fp16': None}[mode]
+    dims = dims_of(config)
+    shapes = dims.shapes()
+    gpu_layers, ref_layers = [], []
+    for i, w in enumerate(layers_w):
+        corr = corrections_for(shapes, seed + 100 + i) if corrected else None
+        packed, opacked = None, None
+        if fmt is not None:
+            packed, opacked = {}, {}
+            for name in sm._PROJECTIONS:
+                g, data, scales = ref.quantize(w[name].numpy(), fmt, None if fmt == 'int8' else group)
+                packed[name] = lb.PackedWeight(tuple(w[name].shape), fmt, g, data, scales)
+                opacked[name] = (tuple(w[name].shape), fmt, g, data, scales)
+        gpu_layers.append(sm.FrozenSmolLayer(config, w, mode=mode, packed_weights=packed, corrections=corr, max_positions=128))
+        ocorr = None if corr is None else {n: c.tensors() for n, c in corr.items()}
+        ref_layers.append(dref.LayerRef(dims, w, opacked, ocorr))
+    model = sm.SmolForCausalLM(sm.FrozenSmolStack(gpu_layers), emb, norm)
+    oracle = dref.DecoderRef(dims, ref_layers, emb, norm, 128)
+    return model, oracle
+
+
+@pytest.mark.parametrize('mode,group,corrected', [('w8a16', None, True), ('w4a16', 64, False), ('nf4a16', 64, True),
+                                                  ('fp16', None, False)])
+def test_layer_prefill_and_decode_match_oracle(mode, group, corrected):
+    model, oracle = build(small_config(layers=1), mode, group, corrected)
+    layer, olayer = model.stack.layers[0], oracle.layers[0]
+    x = (torch.randn(2, 9, 192, generator=torch.Generator().manual_seed(3)) * 0.5).half()
+    y, cache = layer.prefill(x.cuda())
+    ey, ecache = olayer.forward(x, oracle.cos, oracle.sin)
+    assert rel_l2(y, ey) < LAYER_L2
+    assert rel_l2(cache.keys, ecache[0]) < LAYER_L2
+    # three decode steps with the cache, against the oracle's cached decode
+    for t in range(3):
+        xt = (torch.randn(2, 1, 192, generator=torch.Generator().manual_seed(10 + t)) * 0.5).half()
+        y, cache = layer.decode(xt.cuda(), cache)
+        ey, ecache = olayer.forward(xt, oracle.cos, oracle.sin, ecache)
+        assert rel_l2(y, ey) < LAYER_L2, (t, rel_l2(y, ey))
+    assert cache.length == 12
+
+
+def test_layer_matches_reference_fixture(golden):
+    """135M dims, theta 1e5, W8 + rank-32 corrections: the GPU layer against the output the
+    reference's own FrozenSmolLayer.reference_cpu recorded."""
+    import torch_npu_lowbit as lb
+    import torch_npu_smollm as sm
+    from test_oracle_golden import layer_weights, layer_corrections
+    from torch_npu_lowbit_correction import LowRankCorrection
+    z = golden('smollm_layer.npz')
+    weights, x = layer_weights(414)
+    corr = {n: LowRankCorrection(tuple(u.shape[:1]) + tuple(d.shape[1:]), 32, d.numpy().tobytes(), u.numpy().tobytes())
+            for n, (d, u) in layer_corrections(415).items()}
+    packed = {n: lb.PackedWeight(tuple(w.shape), 'int8', w.shape[1], *ref.quantize(w.numpy(), 'int8')[1:])
+              for n, w in weights.items() if w.ndim == 2}
+    config = dict(small_config(layers=1, vocab=49152, hidden=576, heads=9, kv=3, inter=1536, theta=100000.0))
+    layer = sm.FrozenSmolLayer(config, weights, mode='w8a16', packed_weights=packed, corrections=corr, max_positions=64)
+    y, cache = layer.prefill(x.cuda())
+    expected = torch.from_numpy(z['w8corr/y'].view(np.float16))
+    assert rel_l2(y, expected) < LAYER_L2
+    keys = torch.from_numpy(z['w8corr/keys'].view(np.float16))
+    assert rel_l2(cache.keys, keys) < LAYER_L2
+
+
+@pytest.mark.parametrize('config,mode,group,corrected', [
+    (small_config(layers=3), 'w8a16', None, True),
+    (small_config(layers=3), 'nf4a16', 64, True),
+    (small_config(layers=3), 'w4a16', 64, False),
+    (SMOL135, 'w8a16', None, True),
+])
+def test_generate_matches_oracle(config, mode, group, corrected):
+    model, oracle = build(config, mode, group, corrected)
+    ids = torch.randint(0, config['vocab_size'], (2, 16), generator=torch.Generator().manual_seed(5))
+    steps = 32
+    tokens, logits = model.generate(ids.cuda(), steps, return_logits=True)
+    etokens, elogits = oracle.generate(ids, steps)
+    for t in range(steps):
+        assert rel_l2(logits[t], elogits[t]) < LOGIT_L2, (t, rel_l2(logits[t], elogits[t]))
+    assert torch.equal(tokens.cpu(), etokens), (tokens.cpu(), etokens)
+
+
+def test_graph_replay_equals_eager():
+    model, _ = build(small_config(layers=2), 'nf4a16', 64, True)
+    ids = torch.randint(0, 1024, (3, 8), generator=torch.Generator().manual_seed(7)).cuda()
+    a = model.generate(ids, 12, graph=True)
+    b = model.generate(ids, 12, graph=False)
+    assert torch.equal(a, b)
+
+
+def test_snapshots_stay_immutable():
+    model, _ = build(small_config(layers=1), 'w8a16', None, False)
+    layer = model.stack.layers[0]
+    x = (torch.randn(1, 5, 192, generator=torch.Generator().manual_seed(1)) * 0.5).half().cuda()
+    _, c0 = layer.prefill(x)
+    xa = (torch.randn(1, 1, 192, generator=torch.Generator().manual_seed(2)) * 0.5).half().cuda()
+    xb = (torch.randn(1, 1, 192, generator=torch.Generator().manual_seed(3)) * 0.5).half().cuda()
+    ya, ca = layer.decode(xa, c0)
+    yb, cb = layer.decode(xb, c0)          # branch from the same snapshot
+    ya2, _ = layer.decode(xa, c0)
+    assert torch.equal(ya, ya2)
+    assert not torch.equal(ya, yb)
+    assert ca.length == cb.length == 6
+    with pytest.raises(ValueError):
+        layer.decode(x, c0)                # more than one token
+
+
+def test_layer_validation_follows_reference():
+    import torch_npu_smollm as sm
+    layers_w, _, _ = sm.random_smollm_weights(small_config(layers=1))
+    with pytest.raises(ValueError):
+        sm.FrozenSmolLayer(small_config(layers=1), layers_w[0], mode='int3')
+    with pytest.raises(ValueError):
+        sm.FrozenSmolLayer(small_config(layers=1), layers_w[0], mode='nf4a16', fp16_projections=('mlp.down_proj.weight',))
+    layer = sm.FrozenSmolLayer(small_config(layers=1), layers_w[0], mode='w8a16',
+                               fp16_projections=('mlp.down_proj.weight',))
+    assert layer.fp16_projections == frozenset(('mlp.down_proj.weight',))
+    with pytest.raises(ValueError):
+        layer(torch.zeros(1, 2, 192, dtype=torch.float32, device='cuda'))

@@ -36,7 +36,8 @@ cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *res, uint16_t *res_out, const uint16_t *gamma,
                            uint16_t *out, int rows, int dim, float eps, cudaStream_t st);
 cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint16_t *cos_t, const uint16_t *sin_t,
-                        int tokens, int heads, int kvh, int hd, int q_stride, int k_stride, cudaStream_t st);
+                        int table_rows, int tokens, int heads, int kvh, int hd, int q_stride, int k_stride,
+                        cudaStream_t st);
 cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *kc, uint16_t *vc,
                              const int32_t *lengths, int batch, int kvh, int hd, int max_pos, cudaStream_t st);
 size_t attention_smem(int heads, int kvh, int max_pos);
@@ -319,13 +320,13 @@ int lb_rmsnorm(const uint16_t *x, const uint16_t *residual, uint16_t *residual_o
 }
 
 int lb_rope(uint16_t *q, uint16_t *k, const int32_t *positions, const uint16_t *cos_table, const uint16_t *sin_table,
-            int tokens, int heads, int kv_heads, int head_dim, int q_stride, int k_stride, void *stream) {
+            int table_rows, int tokens, int heads, int kv_heads, int head_dim, int q_stride, int k_stride, void *stream) {
   if (injected("lb_rope")) return LB_ERR_INJECTED;
-  if (!q || !k || !positions || !cos_table || !sin_table || tokens < 1 || heads < 1 || kv_heads < 1 || head_dim < 2 ||
-      head_dim % 2 || q_stride < heads * head_dim || k_stride < kv_heads * head_dim)
+  if (!q || !k || !positions || !cos_table || !sin_table || table_rows < 1 || tokens < 1 || heads < 1 ||
+      kv_heads < 1 || head_dim < 2 || head_dim % 2 || q_stride < heads * head_dim || k_stride < kv_heads * head_dim)
     return LB_ERR_INVALID_ARGUMENT;
-  return cuda_status(launch_rope(q, k, positions, cos_table, sin_table, tokens, heads, kv_heads, head_dim, q_stride,
-                                 k_stride, static_cast<cudaStream_t>(stream)));
+  return cuda_status(launch_rope(q, k, positions, cos_table, sin_table, table_rows, tokens, heads, kv_heads, head_dim,
+                                 q_stride, k_stride, static_cast<cudaStream_t>(stream)));
 }
 
 int lb_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *k_cache, uint16_t *v_cache,

@@ -87,8 +87,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half *__restrict__
 // RoPE in place (torch_npu_smollm.py:174-177): v = half(half(v*cos) + half(rot(v)*sin)),
 // rot(v) = cat(-v[hd/2:], v[:hd/2]).  One thread per (token, head, i < hd/2) pair.
 __global__ void rope_kernel(__half *__restrict__ q, __half *__restrict__ k, const int32_t *__restrict__ pos,
-                            const __half *__restrict__ cos_t, const __half *__restrict__ sin_t, int tokens, int heads,
-                            int kv_heads, int hd, int q_stride, int k_stride) {
+                            const __half *__restrict__ cos_t, const __half *__restrict__ sin_t, int table_rows,
+                            int tokens, int heads, int kv_heads, int hd, int q_stride, int k_stride) {
   pdl_launch();
   pdl_wait();
   const int half_d = hd / 2;
@@ -100,6 +100,7 @@ __global__ void rope_kernel(__half *__restrict__ q, __half *__restrict__ k, cons
     const int h = rem / half_d, i = rem % half_d;
     __half *base = h < heads ? q + int64_t(t) * q_stride + h * hd : k + int64_t(t) * k_stride + (h - heads) * hd;
     const int p = pos[t];
+    if (p < 0 || p >= table_rows) continue;
     const __half a = base[i], b = base[i + half_d];
     const __half c0 = cos_t[int64_t(p) * hd + i], s0 = sin_t[int64_t(p) * hd + i];
     const __half c1 = cos_t[int64_t(p) * hd + i + half_d], s1 = sin_t[int64_t(p) * hd + i + half_d];
@@ -305,11 +306,12 @@ cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *res, uint16_t *res
 }
 
 cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint16_t *cos_t, const uint16_t *sin_t,
-                        int tokens, int heads, int kvh, int hd, int q_stride, int k_stride, cudaStream_t st) {
+                        int table_rows, int tokens, int heads, int kvh, int hd, int q_stride, int k_stride,
+                        cudaStream_t st) {
   const int64_t work = int64_t(tokens) * (heads + kvh) * (hd / 2);
   return launch_k(rope_kernel, dim3(grid_1d(work, 256)), dim3(256), 0, st, reinterpret_cast<__half *>(q),
                   reinterpret_cast<__half *>(k), pos, reinterpret_cast<const __half *>(cos_t),
-                  reinterpret_cast<const __half *>(sin_t), tokens, heads, kvh, hd, q_stride, k_stride);
+                  reinterpret_cast<const __half *>(sin_t), table_rows, tokens, heads, kvh, hd, q_stride, k_stride);
 }
 
 cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *kc, uint16_t *vc,

@@ -39,7 +39,7 @@ SIGNATURES = {
     'lb_linear_path': ([_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_select': ([_I, _I, _I, _I, _I, _I], _I),
     'lb_rmsnorm': ([_P, _P, _P, _P, _P, _I, _I, _F, _P], _I),
-    'lb_rope': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
+    'lb_rope': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     'lb_kv_append': ([_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _P], _I),
     'lb_attention_decode': ([_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _S, _P], _I),
     'lb_attention_workspace_bytes': ([_I, _I, _I], _S),

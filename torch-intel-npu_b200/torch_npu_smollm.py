@@ -1,0 +1,510 @@
+"""Frozen SmolLM decoder layers with low-bit projections on B200 (drop-in for torch_npu_smollm).
+
+Keeps the reference module's public surface (torch_npu_smollm.py): ``FrozenSmolLayer``
+(modes fp16 / w8a16 / w4a16 / nf4a16, ``packed_weights``, ``fp16_projections``,
+``corrections``; ``forward`` / ``prefill`` / ``decode``), ``SmolKVCache`` snapshots and
+``FrozenSmolStack`` (``from_checkpoint``, ``forward`` / ``prefill`` / ``decode``).
+
+What changes underneath the API:
+* every projection is one ``lb_linear`` call (decode GEMV / tcgen05 GEMM with the
+  rank-r correction fused), instead of a compiled NPU graph;
+* RMSNorm (fused with the residual add that precedes it), RoPE, the KV append and
+  one-token GQA attention are the library's own kernels and follow the reference's fp16
+  staging (torch_npu_smollm.py:166-193); prefill attention uses PyTorch SDPA;
+* dimensions and RoPE theta come from the config (the reference hard-wires the 135M
+  shape, theta 1e5 and 64 positions; torch_npu_smollm.py:79-83, :111-116);
+* corrections are accepted for every quantized mode (the reference accepts them for
+  w8a16 only, torch_npu_smollm.py:90-93; the correction math is format independent);
+* ``SmolKVCache`` snapshots share one preallocated device buffer; decoding from a stale
+  snapshot copies the buffer first, so snapshots stay immutable as in the reference.
+``SmolForCausalLM`` (not in the reference) adds the tied embedding / LM head and a
+greedy ``generate`` whose decode step is one replayed CUDA graph.
+"""
+from dataclasses import dataclass, field
+import json
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+import lowbit_runtime as rt
+from torch_npu_lowbit import PackedWeight, quantize_weight_device
+from torch_npu_lowbit_correction import LowRankCorrection
+
+_PROJECTIONS = ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight',
+                'self_attn.o_proj.weight', 'mlp.gate_proj.weight', 'mlp.up_proj.weight', 'mlp.down_proj.weight')
+_NORMS = ('input_layernorm.weight', 'post_attention_layernorm.weight')
+_WEIGHT_FORMATS = {'fp16': None, 'w8a16': 'int8', 'w4a16': 'int4', 'nf4a16': 'nf4'}
+
+
+def _projection_policy(mode, names):
+    """torch_npu_smollm.py:31-37."""
+    if (type(names) is not tuple or any(type(name) is not str for name in names)
+            or len(set(names)) != len(names) or not set(names) <= set(_PROJECTIONS)):
+        raise ValueError('fp16_projections requires a tuple of distinct SmolLM projection weight names')
+    if names and (mode != 'w8a16' or len(names) == len(_PROJECTIONS)):
+        raise ValueError('FP16 protection requires w8a16 with at least one INT8 projection; use mode=fp16 for all FP16')
+    return frozenset(names)
+
+
+@dataclass(frozen=True)
+class SmolConfig:
+    hidden: int
+    intermediate: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    eps: float
+    theta: float
+    vocab: int
+    layers: int
+
+    @classmethod
+    def from_dict(cls, config):
+        """Llama-style SmolLM config (the reference requires exactly the 135M values)."""
+        required = dict(model_type='llama', hidden_act='silu', attention_bias=False, mlp_bias=False)
+        if any(config.get(k, v) != v for k, v in required.items()) or config.get('rope_scaling') is not None:
+            raise ValueError('Requires a llama-style SmolLM configuration')
+        hidden, heads = config['hidden_size'], config['num_attention_heads']
+        kv = config.get('num_key_value_heads', heads)
+        if hidden % heads or heads % kv or hidden // heads != 64:
+            raise ValueError('Requires head_dim 64 and grouped KV heads')
+        return cls(hidden, config['intermediate_size'], heads, kv, hidden // heads, float(config.get('rms_norm_eps', 1e-5)),
+                   float(config.get('rope_theta', 10000.0)), int(config.get('vocab_size', 49152)),
+                   int(config.get('num_hidden_layers', 1)))
+
+    def shapes(self):
+        d, f, hd = self.hidden, self.intermediate, self.head_dim
+        q, kv = self.heads * hd, self.kv_heads * hd
+        return {'self_attn.q_proj.weight': (q, d), 'self_attn.k_proj.weight': (kv, d), 'self_attn.v_proj.weight': (kv, d),
+                'self_attn.o_proj.weight': (d, q), 'mlp.gate_proj.weight': (f, d), 'mlp.up_proj.weight': (f, d),
+                'mlp.down_proj.weight': (d, f), 'input_layernorm.weight': (d,), 'post_attention_layernorm.weight': (d,)}
+
+
+def rope_tables(cfg, positions, device):
+    """fp16 cos/sin [positions, head_dim] built like torch_npu_smollm.py:113-116."""
+    hd = cfg.head_dim
+    frequency = 1. / (cfg.theta ** (torch.arange(0, hd, 2).float() / hd))
+    angles = torch.outer(torch.arange(positions).float(), frequency)
+    angles = torch.cat((angles, angles), dim=-1)
+    return angles.cos().half().to(device), angles.sin().half().to(device)
+
+
+@dataclass(eq=False)
+class _CacheStore:
+    keys: torch.Tensor        # [B, kv_heads, max_pos, hd]
+    values: torch.Tensor
+    written: int              # longest prefix any snapshot has written
+
+
+@dataclass(frozen=True, eq=False)
+class SmolKVCache:
+    """KV snapshot (torch_npu_smollm.py:547-555): positions [0, length) are valid."""
+    _owner: object
+    _sequence: object
+    _store: _CacheStore = field(repr=False)
+    length: int
+
+    @property
+    def keys(self):
+        return self._store.keys[:, :, :self.length]
+
+    @property
+    def values(self):
+        return self._store.values[:, :, :self.length]
+
+
+class FrozenSmolLayer(torch.nn.Module):
+    """One decoder layer on the GPU; constructor arguments follow torch_npu_smollm.py:74-117."""
+
+    def __init__(self, config, weights, *, mode='w8a16', packed_weights=None, fp16_projections=(), corrections=None,
+                 group_size=None, device=None, max_positions=None):
+        super().__init__()
+        if mode not in _WEIGHT_FORMATS:
+            raise ValueError('Requires fp16, w8a16, w4a16 or nf4a16')
+        cfg = config if isinstance(config, SmolConfig) else SmolConfig.from_dict(config)
+        self.config = cfg
+        self._mode = mode
+        weight_format = _WEIGHT_FORMATS[mode]
+        self._fp16_projections = _projection_policy(mode, fp16_projections)
+        shapes = cfg.shapes()
+        if set(weights) != set(shapes):
+            raise ValueError('Unexpected layer weight names')
+        if corrections is not None and (type(corrections) is not dict or mode == 'fp16'
+                                        or not set(corrections) <= set(_PROJECTIONS)
+                                        or set(corrections) & self._fp16_projections
+                                        or any(not isinstance(c, LowRankCorrection) or c.shape != shapes[n] or c.rank > 32
+                                               for n, c in corrections.items())):
+            raise ValueError('Corrections require matching rank<=32 factors on quantized, unprotected projections')
+        if packed_weights is not None:
+            if weight_format is None or type(packed_weights) is not dict or set(packed_weights) != set(_PROJECTIONS):
+                raise ValueError('Prepared weights require all seven projections in a matching lowbit mode')
+            for name, q in packed_weights.items():
+                if (not isinstance(q, PackedWeight) or q.shape != shapes[name] or q.format != weight_format
+                        or (weight_format == 'int8' and q.group_size != shapes[name][1])):
+                    raise ValueError('Prepared weights require matching formats/shapes; W8 uses per-row scales')
+        rt.require_cuda()
+        self.device = rt.cuda_device(device)
+        self.max_positions = max_positions or 4096
+        self._proj = {}
+        for name in _PROJECTIONS:
+            w = weights[name]
+            if not isinstance(w, torch.Tensor) or w.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+                raise ValueError('Preparation requires FP16/BF16/FP32 weights')
+            n, k = shapes[name]
+            if weight_format is None or name in self._fp16_projections:
+                codes = w.detach().to(self.device, torch.float16).contiguous().view(torch.uint8).reshape(-1)
+                entry = dict(fmt='fp16', group=k, codes=codes, scales=None, packed=None)
+            elif packed_weights is not None:
+                q = packed_weights[name]
+                codes, scales = q.to_device(self.device)
+                entry = dict(fmt=weight_format, group=q.group_size, codes=codes, scales=scales, packed=q)
+            else:
+                g = k if weight_format == 'int8' else (group_size or 32)
+                half = w.detach().to(self.device, torch.float16)   # reference quantizes w.float().half()
+                codes, scales = quantize_weight_device(half, format=weight_format, group_size=g)
+                entry = dict(fmt=weight_format, group=g, codes=codes, scales=scales, packed=None)
+            entry.update(n=n, k=k, down=None, up=None)
+            if corrections and name in corrections:
+                down, up = corrections[name].tensors()
+                entry['down'], entry['up'] = down.to(self.device), up.to(self.device)
+            self._proj[name] = entry
+        self._norm = {name: weights[name].detach().to(self.device, torch.float16).contiguous() for name in _NORMS}
+        self._owner = object()
+        self.eval()
+
+    mode = property(lambda self: self._mode)
+    fp16_projections = property(lambda self: self._fp16_projections)
+
+    # ---- building blocks -------------------------------------------------------------
+    def linear(self, name, x, out=None):
+        p = self._proj[name]
+        return rt.linear(x, p['fmt'], p['group'], p['n'], p['codes'], p['scales'], down=p['down'], up=p['up'], out=out)
+
+    def norm(self, x, name, residual=None, residual_out=None, out=None):
+        """RMSNorm of x (or of half(x + residual), written to residual_out)."""
+        rows, d = x.shape
+        out = torch.empty_like(x) if out is None else out
+        rt.check(rt.lib().lb_rmsnorm(rt.ptr(x), rt.ptr(residual), rt.ptr(residual_out), rt.ptr(self._norm[name]),
+                                     rt.ptr(out), rows, d, self.config.eps, rt.stream_ptr(x.device)), 'lb_rmsnorm')
+        return out
+
+    def _attention_prefill(self, q, k, v, b, s):
+        """Causal GQA attention for a whole prompt (PyTorch SDPA on the device)."""
+        cfg = self.config
+        q = q.view(b, s, cfg.heads, cfg.head_dim).transpose(1, 2)
+        k = k.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        v = v.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        out = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=1.0 / cfg.head_dim ** 0.5,
+                                             enable_gqa=cfg.heads != cfg.kv_heads)
+        return out.transpose(1, 2).reshape(b * s, cfg.heads * cfg.head_dim)
+
+    def _qkv(self, normed, positions, rope):
+        q = self.linear('self_attn.q_proj.weight', normed)
+        k = self.linear('self_attn.k_proj.weight', normed)
+        v = self.linear('self_attn.v_proj.weight', normed)
+        cfg = self.config
+        cos, sin = rope
+        rt.check(rt.lib().lb_rope(rt.ptr(q), rt.ptr(k), rt.ptr(positions), rt.ptr(cos), rt.ptr(sin), cos.shape[0], q.shape[0],
+                                  cfg.heads, cfg.kv_heads, cfg.head_dim, q.shape[1], k.shape[1], rt.stream_ptr(q.device)),
+                 'lb_rope')
+        return q, k, v
+
+    def _ffn(self, normed):
+        gate = self.linear('mlp.gate_proj.weight', normed)
+        up = self.linear('mlp.up_proj.weight', normed)
+        act = torch.empty_like(gate)
+        rt.check(rt.lib().lb_silu_mul(rt.ptr(gate), rt.ptr(up), gate.shape[1], rt.ptr(act), gate.shape[0], gate.shape[1],
+                                      rt.stream_ptr(gate.device)), 'lb_silu_mul')
+        return self.linear('mlp.down_proj.weight', act)
+
+    def _check_input(self, x):
+        if self.training:
+            raise ValueError('FrozenSmolLayer requires eval; training is unsupported')
+        if (not isinstance(x, torch.Tensor) or x.dtype != torch.float16 or x.ndim != 3 or x.shape[2] != self.config.hidden
+                or x.device != self.device):
+            raise ValueError(f'Requires FP16 (B,S,{self.config.hidden}) input on {self.device}')
+
+    def _rope(self):
+        cache = getattr(self, '_rope_cache', None)
+        if cache is None:
+            cache = rope_tables(self.config, self.max_positions, self.device)
+            self._rope_cache = cache
+        return cache
+
+    def _full(self, x):
+        b, s, d = x.shape
+        h = x.reshape(b * s, d).contiguous()
+        pos = torch.arange(s, device=self.device, dtype=torch.int32).repeat(b)
+        normed = self.norm(h, 'input_layernorm.weight')
+        q, k, v = self._qkv(normed, pos, self._rope())
+        attn = self._attention_prefill(q, k, v, b, s)
+        o = self.linear('self_attn.o_proj.weight', attn)
+        h1 = torch.empty_like(h)
+        normed = self.norm(o, 'post_attention_layernorm.weight', residual=h, residual_out=h1)
+        down = self._ffn(normed)
+        out = torch.empty_like(h)
+        rt.check(rt.lib().lb_add(rt.ptr(h1), rt.ptr(down), rt.ptr(out), out.numel(), rt.stream_ptr(out.device)), 'lb_add')
+        return out.view(b, s, d), k, v
+
+    # ---- public API (torch_npu_smollm.py:449-544) -------------------------------------
+    def forward(self, x):
+        self._check_input(x)
+        return self._full(x)[0]
+
+    def prefill(self, x):
+        """Full prefix; returns the output and a KV snapshot of the prompt."""
+        self._check_input(x)
+        b, s, _ = x.shape
+        out, k, v = self._full(x)
+        cfg = self.config
+        keys = torch.zeros(b, cfg.kv_heads, self.max_positions, cfg.head_dim, dtype=torch.float16, device=self.device)
+        values = torch.zeros_like(keys)
+        keys[:, :, :s] = k.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        values[:, :, :s] = v.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        return out, SmolKVCache(self._owner, object(), _CacheStore(keys, values, s), s)
+
+    def decode(self, x, cache):
+        """Append exactly one token, leaving the previous snapshot valid."""
+        self._check_input(x)
+        if x.shape[1] != 1 or type(cache) is not SmolKVCache or cache._owner is not self._owner:
+            raise ValueError('Decode requires one token and this layer\'s own KV cache')
+        if not 1 <= cache.length < self.max_positions:
+            raise ValueError('KV cache is full or has an invalid length')
+        store = cache._store
+        if store.written > cache.length:       # decoding from an older snapshot: copy on write
+            store = _CacheStore(store.keys.clone(), store.values.clone(), cache.length)
+        b = x.shape[0]
+        lengths = torch.full((b,), cache.length, dtype=torch.int32, device=self.device)
+        h = x.reshape(b, -1).contiguous()
+        out = self.decode_step(h, store.keys, store.values, lengths)
+        store.written = cache.length + 1
+        return out.view(b, 1, -1), SmolKVCache(self._owner, cache._sequence, store, cache.length + 1)
+
+    def decode_step(self, h, k_cache, v_cache, lengths, normed=None):
+        """One token for every sequence: h [B, d] -> output [B, d]; writes K/V at lengths[b]."""
+        cfg = self.config
+        b = h.shape[0]
+        normed = self.norm(h, 'input_layernorm.weight') if normed is None else normed
+        q, k, v = self._qkv(normed, lengths, self._rope())
+        L = rt.lib()
+        st = rt.stream_ptr(h.device)
+        rt.check(L.lb_kv_append(rt.ptr(k), rt.ptr(v), k.shape[1], rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), b,
+                                cfg.kv_heads, cfg.head_dim, self.max_positions, st), 'lb_kv_append')
+        attn = torch.empty(b, cfg.heads * cfg.head_dim, dtype=torch.float16, device=h.device)
+        rt.check(L.lb_attention_decode(rt.ptr(q), q.shape[1], rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), rt.ptr(attn),
+                                       b, cfg.heads, cfg.kv_heads, cfg.head_dim, self.max_positions,
+                                       1.0 / cfg.head_dim ** 0.5, None, 0, st), 'lb_attention_decode')
+        o = self.linear('self_attn.o_proj.weight', attn)
+        h1 = torch.empty_like(h)
+        normed = self.norm(o, 'post_attention_layernorm.weight', residual=h, residual_out=h1)
+        down = self._ffn(normed)
+        out = torch.empty_like(h)
+        rt.check(L.lb_add(rt.ptr(h1), rt.ptr(down), rt.ptr(out), out.numel(), st), 'lb_add')
+        return out
+
+
+class FrozenSmolStack(torch.nn.Module):
+    """Contiguous decoder layers (torch_npu_smollm.py:558-657)."""
+
+    def __init__(self, layers):
+        super().__init__()
+        if not layers or any(not isinstance(l, FrozenSmolLayer) for l in layers):
+            raise ValueError('Requires a nonempty list of FrozenSmolLayer')
+        self.layers = torch.nn.ModuleList(layers)
+        self.eval()
+
+    @classmethod
+    def from_checkpoint(cls, directory, *, start_layer=0, num_layers=2, mode='w8a16', packed_weights=None,
+                        fp16_projections=(), corrections=None, group_size=None, device=None):
+        """Load layers from a SmolLM safetensors checkpoint directory (config.json + model.safetensors)."""
+        _projection_policy(mode, fp16_projections)
+        from safetensors import safe_open
+        directory = Path(directory)
+        config = json.loads((directory / 'config.json').read_text())
+        total = config.get('num_hidden_layers', 0)
+        if (type(start_layer) is not int or type(num_layers) is not int or start_layer < 0 or num_layers <= 0
+                or start_layer + num_layers > total):
+            raise ValueError('Requires a nonempty contiguous checkpoint layer range')
+        layers = []
+        with safe_open(directory / 'model.safetensors', framework='pt', device='cpu') as f:
+            names = list(f.keys())
+            for i in range(start_layer, start_layer + num_layers):
+                prefix = f'model.layers.{i}.'
+                weights = {n[len(prefix):]: f.get_tensor(n) for n in names if n.startswith(prefix)}
+                layers.append(FrozenSmolLayer(config, weights, mode=mode,
+                                              packed_weights=None if packed_weights is None else packed_weights[i],
+                                              fp16_projections=fp16_projections,
+                                              corrections=None if corrections is None else corrections[i],
+                                              group_size=group_size, device=device))
+        return cls(layers)
+
+    @property
+    def num_layers(self):
+        return len(self.layers)
+
+    def forward(self, x):
+        for layer in self.layers:
+            x = layer(x)
+        return x
+
+    def prefill(self, x):
+        caches, sequence = [], object()
+        for layer in self.layers:
+            x, cache = layer.prefill(x)
+            caches.append(SmolKVCache(cache._owner, sequence, cache._store, cache.length))
+        return x, tuple(caches)
+
+    def decode(self, x, caches, *, group_size=None):
+        """group_size is the reference's NPU chain width (1, 2 or 4); accepted and validated only."""
+        if group_size is not None and group_size not in (1, 2, 4):
+            raise ValueError('Decode group_size must be 1, 2 or 4')
+        if type(caches) is not tuple or len(caches) != self.num_layers:
+            raise ValueError('Requires one KV cache per consecutive layer')
+        if any(c.length != caches[0].length or c._sequence is not caches[0]._sequence for c in caches):
+            raise ValueError('Stack KV caches must belong to the same snapshot and position')
+        updated, sequence = [], object()
+        for layer, cache in zip(self.layers, caches):
+            x, cache = layer.decode(x, cache)
+            updated.append(SmolKVCache(cache._owner, sequence, cache._store, cache.length))
+        return x, tuple(updated)
+
+
+class SmolForCausalLM(torch.nn.Module):
+    """Decoder stack + tied fp16 embedding / LM head with greedy generation.
+
+    The embedding lookup and final norm follow FrozenSmolIO (torch_npu_smollm_io.py:45-61);
+    the decode step (all layers + head + argmax) is captured once per batch size in a
+    CUDA graph and replayed per token.
+    """
+
+    def __init__(self, stack, embedding, norm):
+        super().__init__()
+        self.stack = stack
+        self.config = stack.layers[0].config
+        self.device = stack.layers[0].device
+        self.embedding = embedding.detach().to(self.device, torch.float16).contiguous()
+        self.final_norm = norm.detach().to(self.device, torch.float16).contiguous()
+        self._graphs = {}
+
+    @classmethod
+    def from_weights(cls, config, layer_weights, embedding, norm, **layer_options):
+        layers = [FrozenSmolLayer(config, w, **layer_options) for w in layer_weights]
+        return cls(FrozenSmolStack(layers), embedding, norm)
+
+    def embed(self, ids):
+        t = ids.numel()
+        out = torch.empty(t, self.config.hidden, dtype=torch.float16, device=self.device)
+        rt.check(rt.lib().lb_embed(rt.ptr(ids), rt.ptr(self.embedding), rt.ptr(out), t, self.config.hidden,
+                                   self.config.vocab, rt.stream_ptr(self.device)), 'lb_embed')
+        return out
+
+    def head(self, h, residual=None):
+        """Final RMSNorm (fused with the last residual add) + tied LM head -> fp16 logits."""
+        normed = torch.empty_like(h)
+        res_out = torch.empty_like(h) if residual is not None else None
+        rt.check(rt.lib().lb_rmsnorm(rt.ptr(h), rt.ptr(residual), rt.ptr(res_out), rt.ptr(self.final_norm), rt.ptr(normed),
+                                     h.shape[0], h.shape[1], self.config.eps, rt.stream_ptr(self.device)), 'lb_rmsnorm')
+        return rt.linear(normed, 'fp16', self.config.hidden, self.config.vocab, self.embedding.view(torch.uint8).reshape(-1), None)
+
+    def argmax(self, logits, out):
+        rt.check(rt.lib().lb_argmax(rt.ptr(logits), logits.shape[0], logits.shape[1], rt.ptr(out), None, 0,
+                                    rt.stream_ptr(self.device)), 'lb_argmax')
+        return out
+
+    def prefill(self, ids):
+        """ids [B, S] int64 on the device -> (last-position logits [B, V], caches)."""
+        b, s = ids.shape
+        x = self.embed(ids.reshape(-1)).view(b, s, -1)
+        h, caches = self.stack.prefill(x)
+        last = h[:, -1].contiguous()
+        return self.head(last), caches
+
+    def _state(self, b):
+        cfg, layers = self.config, self.stack.layers
+        mp = layers[0].max_positions
+        return dict(
+            ids=torch.zeros(b, dtype=torch.int64, device=self.device),
+            lengths=torch.zeros(b, dtype=torch.int32, device=self.device),
+            keys=[torch.zeros(b, cfg.kv_heads, mp, cfg.head_dim, dtype=torch.float16, device=self.device) for _ in layers],
+            values=[torch.zeros(b, cfg.kv_heads, mp, cfg.head_dim, dtype=torch.float16, device=self.device) for _ in layers],
+            logits=None)
+
+    def _decode_step(self, st):
+        """Embed st['ids'], run every layer at positions st['lengths'], write logits and the
+        greedy next ids, advance the lengths."""
+        h = self.embed(st['ids'])
+        for i, layer in enumerate(self.stack.layers):
+            h = layer.decode_step(h, st['keys'][i], st['values'][i], st['lengths'])
+        logits = self.head(h)
+        st['logits'] = logits
+        self.argmax(logits, st['ids'])
+        st['lengths'] += 1
+        return logits
+
+    def generate(self, ids, steps, *, graph=True, return_logits=False):
+        """Greedy decoding: prefill ``ids`` [B, S] (device int64), then ``steps`` tokens.
+
+        Returns next tokens [B, steps] (and the fp16 logits of each step when asked)."""
+        b, s = ids.shape
+        if s + steps > self.stack.layers[0].max_positions:
+            raise ValueError('prompt + generated tokens exceed max_positions of the KV cache')
+        logits, caches = self.prefill(ids)
+        st = self._state(b)
+        for i, c in enumerate(caches):
+            st['keys'][i][:, :, :s] = c.keys
+            st['values'][i][:, :, :s] = c.values
+        st['lengths'].fill_(s)
+        tokens = torch.empty(b, steps, dtype=torch.int64, device=self.device)
+        all_logits = [] if return_logits else None
+        self.argmax(logits, st['ids'])
+        tokens[:, 0] = st['ids']
+        if return_logits:
+            all_logits.append(logits.clone())
+        step = self._graph_step(b, st) if graph else (lambda: self._decode_step(st))
+        for t in range(1, steps):
+            out = step()
+            tokens[:, t] = st['ids']
+            if return_logits:
+                all_logits.append(out.clone())
+        return (tokens, all_logits) if return_logits else tokens
+
+    def _graph_step(self, b, st):
+        """Capture the decode step for this state once; returns a replay function."""
+        stream = torch.cuda.current_stream(self.device)
+        saved = st['lengths'].clone()
+        ids = st['ids'].clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            self._decode_step(st)            # warm-up: sizes workspaces outside capture
+            st['lengths'].copy_(saved)
+            st['ids'].copy_(ids)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                logits = self._decode_step(st)
+        stream.wait_stream(side)
+        st['graph'] = g
+
+        def replay():
+            g.replay()
+            return logits
+        return replay
+
+
+def random_smollm_weights(config, seed=0, device='cpu', std=0.02):
+    """Random-init SmolLM weights (std 0.02, unit norms) for synthetic benchmarks and tests."""
+    cfg = config if isinstance(config, SmolConfig) else SmolConfig.from_dict(config)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    for _ in range(cfg.layers):
+        w = {}
+        for name, shape in cfg.shapes().items():
+            if len(shape) == 2:
+                w[name] = (torch.randn(shape, generator=gen, device=device) * std).half()
+            else:
+                w[name] = torch.ones(shape, dtype=torch.float16, device=device)
+        layers.append(w)
+    embedding = (torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=device) * std).half()
+    norm = torch.ones(cfg.hidden, dtype=torch.float16, device=device)
+    return layers, embedding, norm
