@@ -106,6 +106,31 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
 int lb_linear_select(int fmt, int group, int m, int n, int k, int rank);
 
 /*
+ * Allocation-free decode GEMV.  No counterpart in the reference (its linear runs inside
+ * an NPU graph session that owns all of its buffers).
+ *
+ * For callers that cannot provide a workspace -- a host application linking this
+ * library whose device memory belongs to an allocator it may not call, or a
+ * latency-critical thread where a first cudaMalloc would block -- this is lb_linear
+ * restricted to the decode GEMV (M <= 16, 16-byte aligned x / codes / y / factors).
+ * Its scratch (correction projection, split-K partials, arrival counters) is one fixed
+ * array of LB_NOALLOC_SCRATCH_BYTES compiled into the library; every GPU that loads the
+ * library holds it until the process exits.  The call allocates nothing; the caller
+ * still passes every input and the output.
+ *   - The first call on a device looks up the array's device address for that device
+ *     (the device that is current); make that first call before any stream capture.
+ *   - Problems whose scratch would not fit return LB_ERR_WORKSPACE; other M return
+ *     LB_ERR_UNSUPPORTED (use lb_linear with a workspace).
+ *   - All calls on a device share the array: calls that can overlap on the GPU (for
+ *     example on two streams without ordering between them) race and must not be made.
+ */
+#define LB_NOALLOC_SCRATCH_BYTES (4u << 20)
+int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, const uint16_t *x,
+                           const uint8_t *codes, const uint16_t *scales, const uint16_t *down,
+                           const uint16_t *up, int rank, const uint16_t *bias, uint16_t *y,
+                           void *stream);
+
+/*
  * SmolLM decoder ops around the projections (torch_npu_smollm.py:142-193 staging,
  * torch_npu_smollm_io.py:45-61).  All fp16, row-major, stream-ordered.
  */

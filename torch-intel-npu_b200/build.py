@@ -13,7 +13,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
 OUT = HERE / 'liblowbit.so'
 INCLUDE = HERE.parent / 'include'
-SOURCES = ['abi.cu', 'quantize.cu', 'gemv.cu', 'tc_gemm.cu', 'decoder_ops.cu']
+SOURCES = ['abi.cu', 'quantize.cu', 'gemv.cu', 'tc_gemm.cu', 'decoder_ops.cu', 'noalloc.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '-lineinfo', '-std=c++17',
          '-Xcompiler', '-fPIC', '-shared', '-cudart', 'shared', '--expt-relaxed-constexpr',

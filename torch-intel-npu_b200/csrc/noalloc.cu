@@ -1,0 +1,97 @@
+// Allocation-free decode GEMV: lb_linear_gemv_noalloc.
+//
+// Some callers of this library cannot hand it a workspace: a host application that
+// links liblowbit through the C ABI with a device-memory budget owned by another
+// allocator it may not call into, or code on a latency-critical thread where a first
+// cudaMalloc would block and synchronise the device.  For them this entry point runs
+// the decode GEMV (M <= 16) with its scratch -- the correction projection z, split-K
+// fp32 partials and arrival counters -- in one fixed array compiled into the library,
+// so a call allocates nothing.
+//
+// The array below lives in every GPU that loads the library until the process exits.
+// Host code must not use its name as a device address (on the host it is only a
+// stand-in symbol); the device address is looked up once per device with
+// cudaGetSymbolAddress while that device is current, on the first call made there.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace lowbit_host {
+bool gemv_supported(int fmt, int group, int m, int n, int k);
+size_t gemv_workspace_bytes(int fmt, int m, int n, int k);
+cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, const uint16_t *v, uint16_t *z,
+                                   cudaStream_t st);
+cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                        const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
+                        uint16_t *y, void *scratch, int *counters, cudaStream_t st);
+}  // namespace lowbit_host
+
+namespace {
+
+// Layout: [0, 16 KiB) arrival counters (4096 ints) | [16 KiB, 20 KiB) z | rest: partials.
+constexpr size_t kCounterBytes = 4096 * sizeof(int);
+constexpr size_t kZOffset = kCounterBytes;
+constexpr size_t kZBytes = 4096;
+constexpr size_t kPartialOffset = kZOffset + kZBytes;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LB_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_setup_mu;
+void *g_scratch_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once per device).
+cudaError_t scratch_address(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_setup_mu);
+  if (!g_scratch_addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return cudaSuccess;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                                      const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
+                                      const uint16_t *bias, uint16_t *y, void *stream) {
+  using namespace lowbit_host;
+  if (!(fmt == LB_FMT_INT4 || fmt == LB_FMT_NF4 || fmt == LB_FMT_INT8 || fmt == LB_FMT_FP16) || m < 1 || n < 1 ||
+      k < 1 || !x || !codes || !y || (fmt != LB_FMT_FP16 && (!scales || group < 1 || group > k || k % group)))
+    return LB_ERR_INVALID_ARGUMENT;
+  if ((down == nullptr) != (up == nullptr) || (down && (rank < 1 || rank > 32 || rank > n || rank > k)))
+    return LB_ERR_INVALID_ARGUMENT;
+  if (fmt == LB_FMT_FP16) group = k;
+  if (!down) rank = 0;
+  if (!gemv_supported(fmt, group, m, n, k) || !aligned16(x) || !aligned16(codes) || !aligned16(y) ||
+      (down && (!aligned16(down) || !aligned16(up))))
+    return LB_ERR_UNSUPPORTED;   // only the decode GEMV (M <= 16, aligned rows) has this variant
+  if (size_t(m) * 32 * 2 > kZBytes ||
+      gemv_workspace_bytes(fmt, m, n, k) > size_t(LB_NOALLOC_SCRATCH_BYTES) - kPartialOffset)
+    return LB_ERR_WORKSPACE;     // the problem needs more scratch than the fixed array holds
+  void *base = nullptr;
+  cudaError_t e = scratch_address(&base);
+  if (e != cudaSuccess) return LB_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *s = static_cast<uint8_t *>(base);
+  int *counters = reinterpret_cast<int *>(s);
+  // The array keeps whatever the previous call left; the counters must start at zero.
+  e = cudaMemsetAsync(counters, 0, kCounterBytes, st);
+  uint16_t *z = nullptr;
+  if (e == cudaSuccess && rank > 0) {
+    z = reinterpret_cast<uint16_t *>(s + kZOffset);
+    e = launch_lowrank_project(m, k, rank, x, down, z, st);
+  }
+  if (e == cudaSuccess)
+    e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, s + kPartialOffset, counters, st);
+  return e == cudaSuccess ? LB_OK : LB_ERR_CUDA;
+}

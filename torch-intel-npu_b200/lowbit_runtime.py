@@ -48,6 +48,7 @@ SIGNATURES = {
     'lb_embed': ([_P, _P, _P, _L, _I, _L, _P], _I),
     'lb_argmax': ([_P, _I, _I, _P, _P, _S, _P], _I),
     'lb_argmax_workspace_bytes': ([_I, _I], _S),
+    'lb_linear_gemv_noalloc': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P], _I),
 }
 
 
