@@ -118,7 +118,11 @@ class FrozenSmolLayer(torch.nn.Module):
     """One decoder layer on the GPU; constructor arguments follow torch_npu_smollm.py:74-117."""
 
     def __init__(self, config, weights, *, mode='w8a16', packed_weights=None, fp16_projections=(), corrections=None,
-                 group_size=None, device=None, max_positions=None):
+                 group_size=None, device=None, max_positions=None, tp_group=None, row_corrections=None):
+        """``tp_group`` (a torch.distributed NCCL group) makes this the per-rank piece of a
+        tensor-parallel layer: ``config``/``weights`` are the rank's shard (see
+        smollm_parallel.shard_layer_weights) and ``row_corrections`` holds the row-parallel
+        projections' (V shard, U) factors."""
         super().__init__()
         if mode not in _WEIGHT_FORMATS:
             raise ValueError('Requires fp16, w8a16, w4a16 or nf4a16')
@@ -170,6 +174,12 @@ class FrozenSmolLayer(torch.nn.Module):
                 entry['down'], entry['up'] = down.to(self.device), up.to(self.device)
             self._proj[name] = entry
         self._norm = {name: weights[name].detach().to(self.device, torch.float16).contiguous() for name in _NORMS}
+        self._tp = tp_group
+        self._row_corr = {}
+        for name, (down, up) in (row_corrections or {}).items():
+            up64 = torch.zeros(up.shape[0], 64, dtype=torch.float16, device=self.device)
+            up64[:, :up.shape[1]] = up.to(self.device, torch.float16)
+            self._row_corr[name] = (down.to(self.device, torch.float16).contiguous(), up64)
         self._owner = object()
         self.eval()
 
@@ -179,7 +189,34 @@ class FrozenSmolLayer(torch.nn.Module):
     # ---- building blocks -------------------------------------------------------------
     def linear(self, name, x, out=None):
         p = self._proj[name]
+        if self._tp is not None and name in ('self_attn.o_proj.weight', 'mlp.down_proj.weight'):
+            return self._row_parallel(name, x)
         return rt.linear(x, p['fmt'], p['group'], p['n'], p['codes'], p['scales'], down=p['down'], up=p['up'], out=out)
+
+    def _row_parallel(self, name, x):
+        """Row-parallel projection: local partial y_r = half(x_r W_r^T) and z_r = x_r V_r^T,
+        one NCCL all-reduce (sum) over both, then y = half(y + half(z U^T)).  z and U are
+        zero-padded to 64 columns so the correction product runs on the linear kernels."""
+        import torch.distributed as dist
+        p = self._proj[name]
+        m, n = x.shape[0], p['n']
+        corr = self._row_corr.get(name)
+        buf = torch.empty(m * n + (m * 64 if corr else 0), dtype=torch.float16, device=x.device)
+        y = buf[:m * n].view(m, n)
+        rt.linear(x, p['fmt'], p['group'], n, p['codes'], p['scales'], out=y)
+        if corr is None:
+            dist.all_reduce(buf, group=self._tp)
+            return y
+        down, up64 = corr
+        r = down.shape[0]
+        z = buf[m * n:].view(m, 64)
+        z.zero_()
+        z[:, :r].copy_(rt.linear(x, 'fp16', x.shape[1], r, down.view(torch.uint8).reshape(-1), None))
+        dist.all_reduce(buf, group=self._tp)
+        delta = rt.linear(z, 'fp16', 64, n, up64.view(torch.uint8).reshape(-1), None)
+        out = torch.empty_like(y)
+        rt.check(rt.lib().lb_add(rt.ptr(y), rt.ptr(delta), rt.ptr(out), out.numel(), rt.stream_ptr(x.device)), 'lb_add')
+        return out
 
     def norm(self, x, name, residual=None, residual_out=None, out=None):
         """RMSNorm of x (or of half(x + residual), written to residual_out)."""
