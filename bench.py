@@ -275,6 +275,102 @@ def e2e_block(cells, steps, warmup, device, stream):
             'd2h_bytes_per_step': total_n * 2, 'ms_per_step': round(t / steps * 1e3, 4)}
 
 
+# ---- SmolLM decode (BASELINE configs[2..4]) ----------------------------------------------
+SMOL = {
+    '135m': dict(model_type='llama', hidden_size=576, intermediate_size=1536, num_attention_heads=9,
+                 num_key_value_heads=3, rms_norm_eps=1e-5, rope_theta=10000.0, vocab_size=49152, num_hidden_layers=30),
+    '360m': dict(model_type='llama', hidden_size=960, intermediate_size=2560, num_attention_heads=15,
+                 num_key_value_heads=5, rms_norm_eps=1e-5, rope_theta=10000.0, vocab_size=49152, num_hidden_layers=32),
+    '1.7b': dict(model_type='llama', hidden_size=2048, intermediate_size=8192, num_attention_heads=32,
+                 num_key_value_heads=32, rms_norm_eps=1e-5, rope_theta=10000.0, vocab_size=49152, num_hidden_layers=24),
+}
+
+
+def int4_groups(config):
+    """INT4 group 128 where K divides by 128, else 64 (K=960 is not a multiple of 128)."""
+    import torch_npu_smollm as sm
+    return {n: (128 if s[1] % 128 == 0 else 64) for n, s in sm.SmolConfig.from_dict(config).shapes().items() if len(s) == 2}
+
+
+def build_smollm(name, mode, group, device, max_positions, rank=0, world=1, pg=None, seed=0):
+    """Random-init SmolLM of the named architecture (std 0.02), rank-32 corrections on every
+    projection, quantized on the GPU; tensor-parallel when world > 1 and pg is given."""
+    import smollm_parallel as sp
+    import torch_npu_smollm as sm
+    from torch_npu_lowbit_correction import LowRankCorrection
+    config = SMOL[name]
+    layers_w, emb, norm = sm.random_smollm_weights(config, seed=seed, device=device)
+    shapes = sm.SmolConfig.from_dict(config).shapes()
+    gen = torch.Generator(device=device).manual_seed(seed + 1)
+    corrections = [{n: LowRankCorrection.from_tensors((torch.randn(RANK, s[1], generator=gen, device=device) * 1e-3).half(),
+                                                      (torch.randn(s[0], RANK, generator=gen, device=device) * 1e-3).half())
+                    for n, s in shapes.items() if len(s) == 2} for _ in layers_w]
+    if pg is not None and world > 1:
+        return sp.build_tp_causal_lm(config, layers_w, emb, norm, mode=mode, group_size=group, corrections=corrections,
+                                     rank=rank, world=world, group=pg, device=device, max_positions=max_positions)
+    layers = [sm.FrozenSmolLayer(config, w, mode=mode, group_size=group, corrections=c, device=device,
+                                 max_positions=max_positions) for w, c in zip(layers_w, corrections)]
+    return sm.SmolForCausalLM(sm.FrozenSmolStack(layers), emb, norm)
+
+
+def decode_run(model, batch, prompt, steps, world, seed=0):
+    """Prefill a seeded prompt, then time ``steps`` graph-replayed greedy decode steps."""
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=model.device).manual_seed(seed)
+    ids = torch.randint(0, model.config.vocab, (batch, prompt), generator=gen, device=model.device)
+    model.prefill_session(ids)
+    for _ in range(3):
+        model.decode_step(batch)                 # captures the decode graph once
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    barrier(world)
+    e[0].record(stream)
+    model.prefill_session(ids)
+    e[1].record(stream)
+    for _ in range(steps):
+        model.decode_step(batch)
+    e[2].record(stream)
+    e[2].synchronize()
+    pre = max_over_ranks(e[0].elapsed_time(e[1]) * 1e-3, world)
+    dec = max_over_ranks(e[1].elapsed_time(e[2]) * 1e-3, world)
+    return pre, dec
+
+
+def decode_block(world, rank, device, pg, quick=False):
+    """Decode tokens/s for BASELINE configs 2 (135M W8, B=1, rank 0 only), 3 (360M INT4 /
+    NF4, B=64 sharded over ranks, no collective) and 4 (1.7B NF4, B=32, tensor-parallel)."""
+    import smollm_parallel as sp
+    out = {}
+    if rank == 0:
+        m = build_smollm('135m', 'w8a16', None, device, 128 + 128 + 8)
+        pre, dec = decode_run(m, 1, 128, 128, 1)
+        out['smollm135m_w8_b1'] = {'tokens_per_s': round(128 / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
+                                   'config': 'configs[2]: 30 layers, W8 + rank-32 on all 7 projections, prompt 128, '
+                                             '128 greedy steps, batch 1, 1 GPU'}
+        del m
+    barrier(world)
+    b0, b1 = sp.batch_shard(64, rank, world)
+    steps = 64 if quick else 256
+    for tag, mode, group in (('int4', 'w4a16', int4_groups(SMOL['360m'])), ('nf4g64', 'nf4a16', 64)):
+        m = build_smollm('360m', mode, group, device, 512 + steps + 8, seed=0)
+        pre, dec = decode_run(m, b1 - b0, 512, steps, world, seed=rank)
+        out[f'smollm360m_{tag}_b64'] = {'tokens_per_s': round(64 * steps / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
+                                        'config': f'configs[3]: 32 layers, {tag} + rank-32, batch 64 sharded over '
+                                                  f'{world} GPU(s), prompt 512, {steps} greedy steps'}
+        del m
+    torch.cuda.empty_cache()
+    steps = 32 if quick else 128
+    m = build_smollm('1.7b', 'nf4a16', 64, device, 2048 + steps + 8, rank=rank, world=world, pg=pg)
+    pre, dec = decode_run(m, 32, 2048, steps, world)
+    prefill_tokens = 32 * 2048
+    out['smollm1.7b_nf4g64_b32'] = {'tokens_per_s': round(32 * steps / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
+                                    'prefill_tokens_per_s': round(prefill_tokens / pre, 1),
+                                    'config': f'configs[4]: 24 layers, NF4 g64 + rank-32, prefill 32x2048, {steps} '
+                                              f'greedy steps, {"tensor-parallel x" + str(world) if world > 1 else "1 GPU"}'}
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def dist_setup():
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
@@ -355,6 +451,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=10)
     ap.add_argument('--impl', default='lowbit', choices=['lowbit', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-decode', action='store_true')
+    ap.add_argument('--quick-decode', action='store_true')
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -384,12 +482,24 @@ def main():
     t = max_over_ranks(t, world)
     per_step = sum(gemv_bytes(1, c['n'], c['k'], c['fmt'], c['g']) for c in cells)
     value = per_step * args.steps * world / t / 1e9
+    launches_per_step_count = launches_per_step(cells)
     e2e = e2e_block(cells, max(10, args.steps // 4), 3, device, stream)
     e2e_v = max_over_ranks(1.0 / max(e2e['value'], 1e-9), world)
     e2e['value'] = round(world / e2e_v, 1) if world > 1 else e2e['value']
     roof = dominant_kernel_roofline(device, stream, peak_gbs)
     roof['peak_kind'] = f'{peak_kind} HBM copy bandwidth (burst)'
-    del graphs
+    del graphs, cells
+    torch.cuda.empty_cache()
+    decode = None
+    if not args.no_decode:
+        pg = None
+        if world > 1:
+            import torch.distributed as dist
+            pg = dist.group.WORLD
+        try:
+            decode = decode_block(world, rank, device, pg, quick=args.quick_decode)
+        except Exception as exc:  # noqa: BLE001  (report, keep the GEMV line)
+            decode = {'error': f'{type(exc).__name__}: {exc}'[:300]}
     if rank != 0:
         if world > 1:
             import torch.distributed as dist
@@ -402,7 +512,9 @@ def main():
             'config': config_block(world),
             'frac_of_hbm_peak': round(value / world / peak_gbs, 4),
             'e2e': e2e, 'roofline': roof, 'clocks': clocks.summary(),
-            'gpu_launches': launches_per_step(cells) * args.steps}
+            'gpu_launches': launches_per_step_count * args.steps}
+    if decode is not None:
+        line['decode'] = decode
     if not args.no_cpu_baseline:
         line['cpu_baseline'] = cpu_baseline_block()
     print(json.dumps(line), flush=True)

@@ -170,3 +170,13 @@ def test_layer_validation_follows_reference():
     assert layer.fp16_projections == frozenset(('mlp.down_proj.weight',))
     with pytest.raises(ValueError):
         layer(torch.zeros(1, 2, 192, dtype=torch.float32, device='cuda'))
+
+
+def test_session_graph_is_reused_across_generate_calls():
+    model, _ = build(small_config(layers=2), 'w4a16', 64, True)
+    ids = torch.randint(0, 1024, (2, 8), generator=torch.Generator().manual_seed(9)).cuda()
+    a = model.generate(ids, 10)
+    graph = model.session(2)['graph']
+    b = model.generate(ids, 10)
+    assert model.session(2)['graph'] is graph
+    assert torch.equal(a, b)

@@ -121,6 +121,7 @@ def shard_layer_weights(weights, packed, corrections, rank, world, config):
 def tp_config(config, world):
     """Per-rank config: heads, kv heads and FFN width divided by the world size."""
     c = dict(config)
+    c['head_dim'] = config.get('head_dim', config['hidden_size'] // config['num_attention_heads'])
     c['num_attention_heads'] = config['num_attention_heads'] // world
     c['num_key_value_heads'] = config.get('num_key_value_heads', config['num_attention_heads']) // world
     c['intermediate_size'] = config['intermediate_size'] // world

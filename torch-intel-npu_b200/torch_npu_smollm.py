@@ -67,9 +67,10 @@ class SmolConfig:
             raise ValueError('Requires a llama-style SmolLM configuration')
         hidden, heads = config['hidden_size'], config['num_attention_heads']
         kv = config.get('num_key_value_heads', heads)
-        if hidden % heads or heads % kv or hidden // heads != 64:
+        head_dim = config.get('head_dim', hidden // heads)   # explicit for tensor-parallel shards
+        if heads % kv or head_dim != 64:
             raise ValueError('Requires head_dim 64 and grouped KV heads')
-        return cls(hidden, config['intermediate_size'], heads, kv, hidden // heads, float(config.get('rms_norm_eps', 1e-5)),
+        return cls(hidden, config['intermediate_size'], heads, kv, head_dim, float(config.get('rms_norm_eps', 1e-5)),
                    float(config.get('rope_theta', 10000.0)), int(config.get('vocab_size', 49152)),
                    int(config.get('num_hidden_layers', 1)))
 
@@ -164,7 +165,8 @@ class FrozenSmolLayer(torch.nn.Module):
                 codes, scales = q.to_device(self.device)
                 entry = dict(fmt=weight_format, group=q.group_size, codes=codes, scales=scales, packed=q)
             else:
-                g = k if weight_format == 'int8' else (group_size or 32)
+                gs = group_size.get(name) if isinstance(group_size, dict) else group_size
+                g = k if weight_format == 'int8' else (gs or 32)
                 half = w.detach().to(self.device, torch.float16)   # reference quantizes w.float().half()
                 codes, scales = quantize_weight_device(half, format=weight_format, group_size=g)
                 entry = dict(fmt=weight_format, group=g, codes=codes, scales=scales, packed=None)
@@ -300,6 +302,16 @@ class FrozenSmolLayer(torch.nn.Module):
         keys[:, :, :s] = k.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
         values[:, :, :s] = v.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
         return out, SmolKVCache(self._owner, object(), _CacheStore(keys, values, s), s)
+
+    def prefill_into(self, x, keys, values):
+        """Prefill writing K/V for positions [0, S) into caller buffers [B, kv_heads, max_pos, hd]."""
+        self._check_input(x)
+        b, s, _ = x.shape
+        out, k, v = self._full(x)
+        cfg = self.config
+        keys[:, :, :s] = k.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        values[:, :, :s] = v.view(b, s, cfg.kv_heads, cfg.head_dim).transpose(1, 2)
+        return out
 
     def decode(self, x, cache):
         """Append exactly one token, leaving the previous snapshot valid."""
@@ -457,15 +469,36 @@ class SmolForCausalLM(torch.nn.Module):
         last = h[:, -1].contiguous()
         return self.head(last), caches
 
-    def _state(self, b):
-        cfg, layers = self.config, self.stack.layers
-        mp = layers[0].max_positions
-        return dict(
-            ids=torch.zeros(b, dtype=torch.int64, device=self.device),
-            lengths=torch.zeros(b, dtype=torch.int32, device=self.device),
-            keys=[torch.zeros(b, cfg.kv_heads, mp, cfg.head_dim, dtype=torch.float16, device=self.device) for _ in layers],
-            values=[torch.zeros(b, cfg.kv_heads, mp, cfg.head_dim, dtype=torch.float16, device=self.device) for _ in layers],
-            logits=None)
+    def session(self, b):
+        """Device state for batch size b, allocated once and reused: token ids, per-sequence
+        lengths, per-layer KV caches [b, kv_heads, max_pos, hd] and the captured decode graph."""
+        st = self._graphs.get(b)
+        if st is None:
+            cfg, layers = self.config, self.stack.layers
+            mp = layers[0].max_positions
+            st = dict(
+                ids=torch.zeros(b, dtype=torch.int64, device=self.device),
+                lengths=torch.zeros(b, dtype=torch.int32, device=self.device),
+                keys=[torch.zeros(b, l.config.kv_heads, mp, cfg.head_dim, dtype=torch.float16, device=self.device)
+                      for l in layers],
+                values=[torch.zeros(b, l.config.kv_heads, mp, cfg.head_dim, dtype=torch.float16, device=self.device)
+                        for l in layers],
+                graph=None, logits=None)
+            self._graphs[b] = st
+        return st
+
+    def prefill_session(self, ids):
+        """Prefill ``ids`` [B, S] into the batch's session: caches filled for [0, S), lengths
+        set to S, ids set to the greedy next token.  Returns the last-position logits."""
+        b, s = ids.shape
+        st = self.session(b)
+        x = self.embed(ids.reshape(-1)).view(b, s, -1)
+        for i, layer in enumerate(self.stack.layers):
+            x = layer.prefill_into(x, st['keys'][i], st['values'][i])
+        logits = self.head(x[:, -1].contiguous())
+        st['lengths'].fill_(s)
+        self.argmax(logits, st['ids'])
+        return logits
 
     def _decode_step(self, st):
         """Embed st['ids'], run every layer at positions st['lengths'], write logits and the
@@ -474,43 +507,23 @@ class SmolForCausalLM(torch.nn.Module):
         for i, layer in enumerate(self.stack.layers):
             h = layer.decode_step(h, st['keys'][i], st['values'][i], st['lengths'])
         logits = self.head(h)
-        st['logits'] = logits
         self.argmax(logits, st['ids'])
         st['lengths'] += 1
         return logits
 
-    def generate(self, ids, steps, *, graph=True, return_logits=False):
-        """Greedy decoding: prefill ``ids`` [B, S] (device int64), then ``steps`` tokens.
+    def decode_step(self, b, graph=True):
+        """One greedy token for every sequence of the batch's session; returns fp16 logits."""
+        st = self.session(b)
+        if not graph:
+            return self._decode_step(st)
+        if st['graph'] is None:
+            self._capture(st)
+        st['graph'].replay()
+        return st['logits']
 
-        Returns next tokens [B, steps] (and the fp16 logits of each step when asked)."""
-        b, s = ids.shape
-        if s + steps > self.stack.layers[0].max_positions:
-            raise ValueError('prompt + generated tokens exceed max_positions of the KV cache')
-        logits, caches = self.prefill(ids)
-        st = self._state(b)
-        for i, c in enumerate(caches):
-            st['keys'][i][:, :, :s] = c.keys
-            st['values'][i][:, :, :s] = c.values
-        st['lengths'].fill_(s)
-        tokens = torch.empty(b, steps, dtype=torch.int64, device=self.device)
-        all_logits = [] if return_logits else None
-        self.argmax(logits, st['ids'])
-        tokens[:, 0] = st['ids']
-        if return_logits:
-            all_logits.append(logits.clone())
-        step = self._graph_step(b, st) if graph else (lambda: self._decode_step(st))
-        for t in range(1, steps):
-            out = step()
-            tokens[:, t] = st['ids']
-            if return_logits:
-                all_logits.append(out.clone())
-        return (tokens, all_logits) if return_logits else tokens
-
-    def _graph_step(self, b, st):
-        """Capture the decode step for this state once; returns a replay function."""
+    def _capture(self, st):
         stream = torch.cuda.current_stream(self.device)
-        saved = st['lengths'].clone()
-        ids = st['ids'].clone()
+        saved, ids = st['lengths'].clone(), st['ids'].clone()
         side = torch.cuda.Stream(self.device)
         side.wait_stream(stream)
         with torch.cuda.stream(side):
@@ -519,14 +532,28 @@ class SmolForCausalLM(torch.nn.Module):
             st['ids'].copy_(ids)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=side):
-                logits = self._decode_step(st)
+                st['logits'] = self._decode_step(st)
         stream.wait_stream(side)
         st['graph'] = g
 
-        def replay():
-            g.replay()
-            return logits
-        return replay
+    def generate(self, ids, steps, *, graph=True, return_logits=False):
+        """Greedy decoding: prefill ``ids`` [B, S] (device int64), then ``steps`` tokens.
+
+        Returns next tokens [B, steps] (and the fp16 logits of each step when asked)."""
+        b, s = ids.shape
+        if s + steps > self.stack.layers[0].max_positions:
+            raise ValueError('prompt + generated tokens exceed max_positions of the KV cache')
+        st = self.session(b)
+        logits = self.prefill_session(ids)
+        tokens = torch.empty(b, steps, dtype=torch.int64, device=self.device)
+        all_logits = [logits.clone()] if return_logits else None
+        tokens[:, 0] = st['ids']
+        for t in range(1, steps):
+            out = self.decode_step(b, graph=graph)
+            tokens[:, t] = st['ids']
+            if return_logits:
+                all_logits.append(out.clone())
+        return (tokens, all_logits) if return_logits else tokens
 
 
 def random_smollm_weights(config, seed=0, device='cpu', std=0.02):
