@@ -30,8 +30,8 @@ cudaError_t launch_linear_generic(int fmt, int group, int m, int n, int k, const
 bool tc_supported(int fmt, int group, int m, int n, int k, int rank);
 size_t tc_partial_bytes(int m, int n, int k);
 cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                      const uint16_t *scales, const uint16_t *z, int ldz_unused, const uint16_t *up, int rank,
-                      const uint16_t *bias, uint16_t *y, int ldy, float *partial, int *err, cudaStream_t st);
+                      const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
+                      uint16_t *y, int ldy, float *partial, int *counters, int *err, cudaStream_t st);
 // decoder_ops.cu
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *res, uint16_t *res_out, const uint16_t *gamma,
                            uint16_t *out, int rows, int dim, float eps, cudaStream_t st);
@@ -121,7 +121,7 @@ int select_path(int fmt, int group, int m, int n, int k, int rank) {
 size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * 32 * 2) : 0; }
 
 // z projection for the TC path at larger M runs on the tensor cores too
-bool z_on_tc(int m, int k, int rank) { return m > 16 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0); }
+bool z_on_tc(int m, int k, int rank) { return m > 32 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0); }
 
 size_t linear_ws(int path, int fmt, int group, int m, int n, int k, int rank) {
   size_t b = kHeader + z_bytes(m, rank);
@@ -268,8 +268,8 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
       float *zpart = reinterpret_cast<float *>(rest + align256(tc_partial_bytes(m, n, k)));
       e = cudaMemsetAsync(z, 0, size_t(m) * 32 * 2, st);
       if (e == cudaSuccess)
-        e = launch_tc(LB_FMT_FP16, k, m, rank, k, x, reinterpret_cast<const uint8_t *>(down), nullptr, nullptr, 0,
-                      nullptr, 0, nullptr, z, 32, zpart, err, st);
+        e = launch_tc(LB_FMT_FP16, k, m, rank, k, x, reinterpret_cast<const uint8_t *>(down), nullptr, nullptr,
+                      nullptr, 0, nullptr, z, 32, zpart, reinterpret_cast<int *>(ws + kCounterOffset), err, st);
     } else {
       e = launch_lowrank_project(m, k, rank, x, down, z, st);
     }
@@ -281,8 +281,8 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
                       reinterpret_cast<int *>(ws + kCounterOffset), st);
       break;
     case LB_PATH_TC:
-      e = launch_tc(fmt, group, m, n, k, x, codes, scales, z, 32, up, rank, bias, y, n,
-                    reinterpret_cast<float *>(rest), err, st);
+      e = launch_tc(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, n, reinterpret_cast<float *>(rest),
+                    reinterpret_cast<int *>(ws + kCounterOffset), err, st);
       break;
     default: e = launch_linear_generic(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, st); break;
   }
@@ -349,7 +349,7 @@ int lb_attention_decode(const uint16_t *q, int q_stride, const uint16_t *k_cache
       heads / kv_heads > 8 || head_dim != 64 || max_pos < 1 || q_stride < heads * head_dim ||
       attention_smem(heads, kv_heads, max_pos) > 160 * 1024)
     return LB_ERR_INVALID_ARGUMENT;
-  if (!aligned16(k_cache) || !aligned16(v_cache)) return LB_ERR_INVALID_ARGUMENT;
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q) || q_stride % 8) return LB_ERR_INVALID_ARGUMENT;
   return cuda_status(launch_attention_decode(q, q_stride, k_cache, v_cache, lengths, out, batch, heads, kv_heads,
                                              head_dim, max_pos, scale, static_cast<cudaStream_t>(stream)));
 }

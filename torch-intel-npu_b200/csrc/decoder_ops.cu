@@ -130,55 +130,65 @@ __global__ void kv_append_kernel(const __half *__restrict__ k, const __half *__r
 
 // One-token GQA attention with the reference staging (torch_npu_smollm.py:178-182):
 // s_j = half(half(q.k_j) * scale); p = half(softmax_f32(s)); out = half(sum_j p_j v_j).
-// One CTA per (batch, kv head) serving the `rep` query heads that share it.
-template <int HD>
+// One CTA per (batch, kv head) serving the REP query heads that share it.  Keys and values
+// are read as 16-byte pieces (8 lanes per 128-byte row, 4 rows per warp) with kUnroll rows
+// per lane in flight, so a CTA keeps ~128 rows of loads outstanding per phase.
+template <int HD, int REP>
 __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__restrict__ q, int q_stride,
                                                                const __half *__restrict__ kc,
                                                                const __half *__restrict__ vc,
                                                                const int32_t *__restrict__ lengths,
                                                                __half *__restrict__ out, int heads, int kvh,
                                                                int max_pos, float scale) {
-  extern __shared__ float sc[];  // [rep][len]
+  static_assert(HD == 64, "rows are 8 lanes x 8 halves");
+  constexpr int kUnroll = 4;
+  extern __shared__ float sc[];  // [REP][max_pos]
   __shared__ float sh[32];
-  __shared__ float outp[8][8][HD];  // [warp][rep][dim] partials (rep <= 8)
+  __shared__ float outp[8][REP][HD];
   pdl_launch();
   pdl_wait();
   const int b = blockIdx.x / kvh, g = blockIdx.x % kvh;
-  const int rep = heads / kvh;
   const int len = min(lengths[b] + 1, max_pos);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int sub = lane >> 3, l8 = lane & 7;
   const __half *kbase = kc + (int64_t(b) * kvh + g) * max_pos * HD;
   const __half *vbase = vc + (int64_t(b) * kvh + g) * max_pos * HD;
-  // scores: 8 lanes per key row (16 bytes each), 4 keys per warp per step
-  const int sub = lane >> 3, l8 = lane & 7;
-  float qv[8][8];
-  for (int r = 0; r < rep; ++r) {
-    const __half *qr = q + int64_t(b) * q_stride + (g * rep + r) * HD + l8 * 8;
+  float qv[REP][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) qv[r][j] = __half2float(qr[j]);
+  for (int r = 0; r < REP; ++r) {
+    const uint4 qq = *reinterpret_cast<const uint4 *>(q + int64_t(b) * q_stride + (g * REP + r) * HD + l8 * 8);
+    const __half *qh = reinterpret_cast<const __half *>(&qq);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qv[r][e] = __half2float(qh[e]);
   }
-  for (int j0 = warp * 4; j0 < len; j0 += nw * 4) {
-    const int j = j0 + sub;
-    float d[8];
+  // ---- scores -------------------------------------------------------------------------
+  for (int j0 = warp * 4 * kUnroll; j0 < len; j0 += nw * 4 * kUnroll) {
+    uint4 kv[kUnroll];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) d[r] = 0.f;
-    if (j < len) {
-      const uint4 kv = *reinterpret_cast<const uint4 *>(kbase + int64_t(j) * HD + l8 * 8);
-      const __half *kh = reinterpret_cast<const __half *>(&kv);
-      for (int r = 0; r < rep; ++r)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d[r] = fmaf(qv[r][e], __half2float(kh[e]), d[r]);
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = j0 + u * 4 + sub;
+      kv[u] = j < len ? *reinterpret_cast<const uint4 *>(kbase + int64_t(j) * HD + l8 * 8) : make_uint4(0, 0, 0, 0);
     }
-    for (int r = 0; r < rep; ++r) {
-      float s = d[r];
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      if (l8 == 0 && j < len) sc[r * max_pos + j] = __half2float(__float2half_rn(__half2float(__float2half_rn(s)) * scale));
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = j0 + u * 4 + sub;
+      const __half *kh = reinterpret_cast<const __half *>(&kv[u]);
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d = fmaf(qv[r][e], __half2float(kh[e]), d);
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        d += __shfl_xor_sync(0xffffffffu, d, 4);
+        if (l8 == 0 && j < len) sc[r * max_pos + j] = __half2float(__float2half_rn(__half2float(__float2half_rn(d)) * scale));
+      }
     }
   }
   __syncthreads();
-  for (int r = 0; r < rep; ++r) {
+  // ---- softmax in fp32, probabilities rounded to fp16 ----------------------------------
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
     float mx = -INFINITY;
     for (int j = threadIdx.x; j < len; j += blockDim.x) mx = fmaxf(mx, sc[r * max_pos + j]);
     mx = block_max(mx, sh);
@@ -193,29 +203,54 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__r
       sc[r * max_pos + j] = __half2float(__float2half_rn(__fdiv_rn(sc[r * max_pos + j], sum)));
   }
   __syncthreads();
-  // out: each warp a strided range of keys, lane covers 2 dims (HD = 64)
-  float acc[8][2];
+  // ---- out = p . V: lane covers 8 dims of one row, 4 rows per warp per step ------------
+  float acc[REP][8];
 #pragma unroll
-  for (int r = 0; r < 8; ++r) acc[r][0] = acc[r][1] = 0.f;
-  for (int j = warp; j < len; j += nw) {
-    const __half2 vv = *reinterpret_cast<const __half2 *>(vbase + int64_t(j) * HD + 2 * lane);
-    const float2 vf = __half22float2(vv);
-    for (int r = 0; r < rep; ++r) {
-      const float pj = sc[r * max_pos + j];
-      acc[r][0] = fmaf(pj, vf.x, acc[r][0]);
-      acc[r][1] = fmaf(pj, vf.y, acc[r][1]);
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
+  for (int j0 = warp * 4 * kUnroll; j0 < len; j0 += nw * 4 * kUnroll) {
+    uint4 vv[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = j0 + u * 4 + sub;
+      vv[u] = j < len ? *reinterpret_cast<const uint4 *>(vbase + int64_t(j) * HD + l8 * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = j0 + u * 4 + sub;
+      if (j >= len) continue;
+      const __half *vh = reinterpret_cast<const __half *>(&vv[u]);
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const float pj = sc[r * max_pos + j];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[r][e] = fmaf(pj, __half2float(vh[e]), acc[r][e]);
+      }
     }
   }
-  for (int r = 0; r < rep; ++r) {
-    outp[warp][r][2 * lane] = acc[r][0];
-    outp[warp][r][2 * lane + 1] = acc[r][1];
+  // reduce the 4 row groups of the warp (lanes l8, l8+8, l8+16, l8+24), then across warps
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = acc[r][e];
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      acc[r][e] = v;
+    }
+  if (sub == 0) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) outp[warp][r][l8 * 8 + e] = acc[r][e];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < rep * HD; i += blockDim.x) {
+  for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
     const int r = i / HD, dd = i % HD;
-    float s = 0.f;
-    for (int w = 0; w < nw; ++w) s += outp[w][r][dd];
-    out[int64_t(b) * heads * HD + (g * rep + r) * HD + dd] = __float2half_rn(s);
+    float s2 = 0.f;
+    for (int w = 0; w < nw; ++w) s2 += outp[w][r][dd];
+    out[int64_t(b) * heads * HD + (g * REP + r) * HD + dd] = __float2half_rn(s2);
   }
 }
 
@@ -324,17 +359,34 @@ cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride
 
 size_t attention_smem(int heads, int kvh, int max_pos) { return size_t(heads / kvh) * max_pos * sizeof(float); }
 
-cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
-                                    const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
-                                    int max_pos, float scale, cudaStream_t st) {
-  if (hd != 64) return cudaErrorInvalidValue;
-  const size_t smem = attention_smem(heads, kvh, max_pos);
-  auto kern = attention_decode_kernel<64>;
+template <int REP>
+static cudaError_t launch_attention_rep(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
+                                        const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh,
+                                        int max_pos, float scale, size_t smem, cudaStream_t st) {
+  auto kern = attention_decode_kernel<64, REP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   return launch_k(kern, dim3(batch * kvh), dim3(256), smem, st, reinterpret_cast<const __half *>(q), q_stride,
                   reinterpret_cast<const __half *>(kc), reinterpret_cast<const __half *>(vc), lengths,
                   reinterpret_cast<__half *>(out), heads, kvh, max_pos, scale);
+}
+
+cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
+                                    const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
+                                    int max_pos, float scale, cudaStream_t st) {
+  if (hd != 64) return cudaErrorInvalidValue;
+  const size_t smem = attention_smem(heads, kvh, max_pos);
+  switch (heads / kvh) {
+    case 1: return launch_attention_rep<1>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 2: return launch_attention_rep<2>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 3: return launch_attention_rep<3>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 4: return launch_attention_rep<4>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 5: return launch_attention_rep<5>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 6: return launch_attention_rep<6>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 7: return launch_attention_rep<7>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    case 8: return launch_attention_rep<8>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,

@@ -133,7 +133,7 @@ template <int FMT, int BM> struct TcLayout {
   static constexpr int OFF_C = ((OFF_B2 + B2_BYTES + 1023) / 1024) * 1024;
   static constexpr int OFF_LUT = OFF_C + S * C_BYTES;
   static constexpr int OFF_BAR = ((OFF_LUT + LUT_BYTES + 15) / 16) * 16;
-  static constexpr int BAR_BYTES = (3 * S + 2) * 8 + 16;
+  static constexpr int BAR_BYTES = (3 * S + 2) * 8 + 32;
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
 };
 
@@ -147,7 +147,8 @@ struct TcParams {
   const __half *scales;
   const __half *bias;
   __half *y;
-  float *partial;     // [splits, m, n] when splits > 1
+  float *partial;     // [splits (+1 correction), m, n] fp32 when splits > 1
+  int *counters;      // per-output-tile arrival counters (zero between calls)
   int *err;           // workspace error flag
 };
 
@@ -155,8 +156,11 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return uint32_t((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+constexpr int kDequantWarps = 8;
+constexpr int kTcThreads = 32 * (2 + kDequantWarps);
+
 template <int FMT, int BM>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_z,
                      const TcParams p) {
@@ -186,7 +190,7 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(bar_full_tma + 8 * s, 1);
-      mbar_init(bar_full_a + 8 * s, 4);   // one arrive per dequant warp
+      mbar_init(bar_full_a + 8 * s, kDequantWarps);   // one arrive per dequant warp
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_corr, 1);
@@ -264,38 +268,43 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // --------------------- dequant (mainloop) + epilogue ----------------------
-    const int t = threadIdx.x - 64;      // 0..127: weight row within the tile
-    const int row = 32 * (warp & 3) + lane;  // TMEM lane this warp may access
+    // kDequantWarps warps: thread t handles weight row (t % 128) and the (t / 128)-th
+    // 32-element half of each 64-wide stage, so every SM sub-partition runs two dequant
+    // warps and the code-to-fp16 latency of one hides behind the other.
+    const int t = threadIdx.x - 64;
+    const int drow = t & 127, part = t >> 7;
     if (kDequant) {
-      const int n = n0 + t;
+      const int n = n0 + drow;
       const bool nok = n < p.n;
       const int gpr = p.k / p.group;
       const bool per_row = FMT == LB_FMT_INT8 && p.group == p.k;
       const uint32_t *lut = reinterpret_cast<const uint32_t *>(smem + L::OFF_LUT) + lane;
-      auto load_scales = [&](int kst, __half2 &sa, __half2 &sb) {
-        if (per_row || !nok) { sa = sb = __float2half2_rn(1.f); return; }
-        const int g0 = (kst * 64) / p.group, g1 = (kst * 64 + 32) / p.group;
-        const __half a = p.scales[int64_t(n) * gpr + g0], b = p.scales[int64_t(n) * gpr + g1];
-        sa = __halves2half2(a, a);
-        sb = __halves2half2(b, b);
+      // scales for the next kScaleAhead stages are in flight while the current one dequantizes
+      constexpr int kScaleAhead = 4;
+      __half2 ring[kScaleAhead];
+      auto load_scale = [&](int i) -> __half2 {
+        if (per_row || !nok || i >= nst) return __float2half2_rn(1.f);
+        const __half v = p.scales[int64_t(n) * gpr + ((st_begin + i) * 64 + part * 32) / p.group];
+        return __halves2half2(v, v);
       };
-      __half2 sa, sb, na, nb;
       pdl_wait();
-      if (nst > 0) load_scales(st_begin, na, nb);
+#pragma unroll
+      for (int j = 0; j < kScaleAhead; ++j) ring[j] = load_scale(j);
       for (int i = 0; i < nst; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
-        sa = na; sb = nb;
-        if (i + 1 < nst) load_scales(st_begin + i + 1, na, nb);
+        const __half2 sc = ring[0];
+#pragma unroll
+        for (int j = 0; j + 1 < kScaleAhead; ++j) ring[j] = ring[j + 1];
+        ring[kScaleAhead - 1] = load_scale(i + kScaleAhead);
         if (!mbar_wait(bar_full_tma + 8 * s, ph, abort_flag)) break;
-        const uint8_t *crow = smem + L::OFF_C + s * L::C_BYTES + t * TcFmt<FMT>::CODE_BYTES;
+        const uint8_t *crow = smem + L::OFF_C + s * L::C_BYTES + drow * TcFmt<FMT>::CODE_BYTES;
         uint8_t *abuf = smem + L::OFF_A + s * L::A_BYTES;
         if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
-          const uint4 c0 = *reinterpret_cast<const uint4 *>(crow);
-          const uint4 c1 = *reinterpret_cast<const uint4 *>(crow + 16);
-          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * part);
+          const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
+          for (int w = 0; w < 4; ++w) {
             uint32_t o[4];
             if constexpr (FMT == LB_FMT_INT4) {
               uint32_t q[4];
@@ -311,20 +320,19 @@ __global__ void __launch_bounds__(192, 1)
               o[2] = lut[(b >> 11) & 0x1FE0u];
               o[3] = lut[(b >> 19) & 0x1FE0u];
             }
-            const __half2 sc = w < 4 ? sa : sb;
 #pragma unroll
             for (int j = 0; j < 4; ++j) o[j] = h2_as_u32(__hmul2(u32_as_h2(o[j]), sc));
-            *reinterpret_cast<uint4 *>(abuf + swz128(t, w)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4 *>(abuf + swz128(drow, part * 4 + w)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
-        } else {  // INT8: 64 bytes -> 8 chunks of 8 halves
-          uint32_t wv[16];
+        } else {  // INT8: this thread's 32 bytes -> 4 chunks of 8 halves
+          uint32_t wv[8];
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * v);
+          for (int v = 0; v < 2; ++v) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 32 * part + 16 * v);
             wv[4 * v] = c.x; wv[4 * v + 1] = c.y; wv[4 * v + 2] = c.z; wv[4 * v + 3] = c.w;
           }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < 4; ++j) {
             uint32_t a[2], b[2], o[4];
             int8_word_to_h2(wv[2 * j], a);       // (e0,e2) (e1,e3)
             int8_word_to_h2(wv[2 * j + 1], b);   // (e4,e6) (e5,e7)
@@ -333,11 +341,10 @@ __global__ void __launch_bounds__(192, 1)
             o[2] = __byte_perm(b[0], b[1], 0x5410);
             o[3] = __byte_perm(b[0], b[1], 0x7632);
             if (!per_row) {
-              const __half2 sc = j < 4 ? sa : sb;
 #pragma unroll
               for (int q = 0; q < 4; ++q) o[q] = h2_as_u32(__hmul2(u32_as_h2(o[q]), sc));
             }
-            *reinterpret_cast<uint4 *>(abuf + swz128(t, j)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4 *>(abuf + swz128(drow, part * 4 + j)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         fence_async_smem();
@@ -351,14 +358,19 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------- epilogue ---------------------------------
     const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_acc, 0, abort_flag));
     tc_fence_after();
+    const int row = 32 * (warp & 3) + lane;          // TMEM lane this warp may access
+    // two warps per TMEM lane quadrant split the BM columns; a 16-column tile stays whole
+    constexpr int kColsPerWarp = BM >= 32 ? BM / 2 : BM;
+    const int chalf = (warp - 2) / 4;
+    const int n = n0 + row;
+    float rs = 1.f;
+    if (FMT == LB_FMT_INT8 && p.group == p.k && n < p.n) rs = __half2float(p.scales[n]);
+    const float bias = (p.bias && n < p.n) ? __half2float(p.bias[n]) : 0.f;
+    const int64_t mn = int64_t(p.m) * p.n;
     if (ok) {
-      const int n = n0 + row;
-      float rs = 1.f;
-      if (FMT == LB_FMT_INT8 && p.group == p.k && n < p.n) rs = __half2float(p.scales[n]);
-      const float bias = (p.bias && n < p.n) ? __half2float(p.bias[n]) : 0.f;
       const uint32_t lane_off = uint32_t(32 * (warp & 3)) << 16;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BM; c0 += 16) {
+      for (int c0 = chalf * kColsPerWarp; c0 < (chalf + 1) * kColsPerWarp && c0 < BM; c0 += 16) {
         uint32_t a[16], d[16];
         tmem_ld16(tmem_acc + lane_off + c0, a);
         if (corr) tmem_ld16(tmem_corr + lane_off + c0, d);
@@ -368,10 +380,10 @@ __global__ void __launch_bounds__(192, 1)
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c0 + j;
             if (m >= p.m) break;
-            float v = __uint_as_float(a[j]) * rs;
+            const float v = __uint_as_float(a[j]) * rs;
             if (p.splits > 1) {
-              p.partial[(int64_t(split) * p.m + m) * p.n + n] = v;
-              if (corr) p.partial[(int64_t(p.splits) * p.m + m) * p.n + n] = __uint_as_float(d[j]);
+              p.partial[split * mn + int64_t(m) * p.n + n] = v;
+              if (corr) p.partial[p.splits * mn + int64_t(m) * p.n + n] = __uint_as_float(d[j]);
               continue;
             }
             __half yq = __float2half_rn(v);
@@ -382,6 +394,32 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
+    if (p.splits > 1) {
+      // split-K: the last CTA of this output tile to arrive sums the fp32 partials in split
+      // order (deterministic) and applies the epilogue; it leaves the counter at zero.
+      int *is_last = reinterpret_cast<int *>(const_cast<int *>(abort_flag)) + 1;
+      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kDequantWarps));
+      if (threadIdx.x == 64) *is_last = atomicAdd(p.counters + tile, 1) == p.splits - 1;
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kDequantWarps));
+      if (*is_last) {
+        __threadfence();
+        for (int c = chalf * kColsPerWarp; c < (chalf + 1) * kColsPerWarp && c < BM; ++c) {
+          const int m = m0 + c;
+          if (m >= p.m || n >= p.n) continue;
+          float v = 0.f;
+          for (int sp = 0; sp < p.splits; ++sp) v += __ldcg(p.partial + sp * mn + int64_t(m) * p.n + n);
+          __half yq = __float2half_rn(v);
+          if (p.bias) yq = __float2half_rn(__half2float(yq) + bias);
+          if (p.has_corr)
+            yq = __float2half_rn(__half2float(yq) +
+                                 __half2float(__float2half_rn(__ldcg(p.partial + p.splits * mn + int64_t(m) * p.n + n))));
+          p.y[int64_t(m) * p.ldy + n] = yq;
+        }
+        if (threadIdx.x == 64) p.counters[tile] = 0;
+      }
+    }
   }
 
   tc_fence_before();
@@ -390,32 +428,6 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
-  }
-}
-
-// Sum split-K partials and apply the reference epilogue.  When has_corr, slice
-// [splits] of the partial buffer holds the fp32 correction accumulator z . U^T.
-// One thread per 4 consecutive outputs of a row.
-__global__ void tc_finalize_kernel(int m, int n, int splits, int has_corr, const float *__restrict__ partial,
-                                   const __half *__restrict__ bias, __half *__restrict__ y, int ldy) {
-  pdl_launch();
-  pdl_wait();
-  const int64_t total = int64_t(m) * n;
-  const int nq = (n + 3) / 4;
-  for (int64_t q = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; q < int64_t(m) * nq; q += int64_t(gridDim.x) * blockDim.x) {
-    const int mm = int(q / nq), n0 = int(q % nq) * 4;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int nn = n0 + j;
-      if (nn >= n) break;
-      const int64_t i = int64_t(mm) * n + nn;
-      float v = 0.f;
-      for (int s = 0; s < splits; ++s) v += partial[int64_t(s) * total + i];
-      __half yq = __float2half_rn(v);
-      if (bias) yq = __float2half_rn(__half2float(yq) + __half2float(bias[nn]));
-      if (has_corr) yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(partial[int64_t(splits) * total + i])));
-      y[int64_t(mm) * ldy + nn] = yq;
-    }
   }
 }
 
@@ -475,6 +487,7 @@ int tc_splits(int m, int n, int k) {
   const int tiles = ((n + 127) / 128) * ((m + bm - 1) / bm);
   const int stages = k / 64;
   int s = 1;
+  if (tiles > 4096) return 1;   // the arrival counters live in a fixed 4096-entry region
   while (tiles * s * 2 <= 2 * 148 && stages / (s * 2) >= 4) s *= 2;
   return s;
 }
@@ -491,7 +504,7 @@ static cudaError_t launch_tc_t(const CUtensorMap &w, const CUtensorMap &x, const
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   if (e != cudaSuccess) return e;
   dim3 grid((p.n + 127) / 128, (p.m + BM - 1) / BM, p.splits);
-  return launch_k(kern, grid, dim3(192), size_t(L::TOTAL), st, w, x, u, z, p);
+  return launch_k(kern, grid, dim3(kTcThreads), size_t(L::TOTAL), st, w, x, u, z, p);
 }
 
 template <int FMT>
@@ -509,9 +522,8 @@ static cudaError_t launch_tc_f(int bm, const CUtensorMap &w, const CUtensorMap &
 // y = x . W^T with the reference epilogue.  z (if non-null) is [m, 32] fp16 in device
 // memory, up is U [n, rank].  partial: fp32 scratch of tc_partial_bytes(); err: int flag.
 cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                      const uint16_t *scales, const uint16_t *z, int ldz_unused, const uint16_t *up, int rank,
-                      const uint16_t *bias, uint16_t *y, int ldy, float *partial, int *err, cudaStream_t st) {
-  (void)ldz_unused;
+                      const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
+                      uint16_t *y, int ldy, float *partial, int *counters, int *err, cudaStream_t st) {
   const int bm = tc_block_m(m);
   int splits = tc_splits(m, n, k);
   {
@@ -550,6 +562,7 @@ cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x
   p.bias = reinterpret_cast<const __half *>(bias);
   p.y = reinterpret_cast<__half *>(y);
   p.partial = partial;
+  p.counters = counters;
   p.err = err;
   cudaError_t e;
   switch (fmt) {
@@ -558,12 +571,7 @@ cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x
     case LB_FMT_INT8: e = launch_tc_f<LB_FMT_INT8>(bm, tw, tx, tu, tz, p, st); break;
     default: e = launch_tc_f<LB_FMT_FP16>(bm, tw, tx, tu, tz, p, st); break;
   }
-  if (e != cudaSuccess || p.splits == 1) return e;
-  const int64_t total = int64_t(m) * ((n + 3) / 4);
-  int blocks = int((total + 255) / 256);
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  return launch_k(tc_finalize_kernel, dim3(blocks), dim3(256), 0, st, m, n, p.splits, p.has_corr, (const float *)partial,
-                  reinterpret_cast<const __half *>(bias), reinterpret_cast<__half *>(y), ldy);
+  return e;
 }
 
 }  // namespace lowbit_host
