@@ -33,9 +33,11 @@ static __constant__ float c_nf4[16] = {
     .24611230194568634f, .33791524171829224f, .44070982933044434f, .5626170039176941f, .7229568362236023f, 1.f};
 
 // Fill the per-lane-replicated byte->half2 NF4 table used by the decode and GEMM
-// kernels: word (e * 32 + l) = (NF4h[e & 15], NF4h[e >> 4]) for every lane l.  Each
-// thread writes whole 128-byte entries with 16-byte stores rotated by lane, so the
-// stores of a warp hit distinct bank groups.
+// kernels: word (e * STRIDE + l) = (NF4h[e & 15], NF4h[e >> 4]) for every lane l < 32
+// (STRIDE = 32 packs the entries; 64 leaves a 128-byte gap so that one byte_perm forms
+// the address).  Each thread writes whole entries with 16-byte stores rotated by lane,
+// so the stores of a warp hit distinct bank groups.
+template <int STRIDE = 32>
 __device__ __forceinline__ void fill_nf4_pair_lut(uint32_t *lut) {
   const int lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < 256; e += blockDim.x) {
@@ -43,7 +45,7 @@ __device__ __forceinline__ void fill_nf4_pair_lut(uint32_t *lut) {
     const uint32_t u = h2_as_u32(v);
     const uint4 q = make_uint4(u, u, u, u);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) reinterpret_cast<uint4 *>(lut + e * 32)[(j + lane) & 7] = q;
+    for (int j = 0; j < 8; ++j) reinterpret_cast<uint4 *>(lut + e * STRIDE)[(j + lane) & 7] = q;
   }
 }
 
@@ -112,6 +114,51 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
+
+// ---- mbarriers (bounded waits) and bulk copies --------------------------------------
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false if the CTA aborted or the wait timed out.
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(a, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(a, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) { *abort_flag = 1; return false; }
+  }
+  return true;
+}
+
+// Time-bounded wait that ignores the abort flag (used to drain copies in flight).
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t a, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(a, parity))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

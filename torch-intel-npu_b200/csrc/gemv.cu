@@ -22,19 +22,13 @@
 #include <cstdio>
 #include <cstdlib>
 
-#include "common.cuh"
+#include "gemv_frag.cuh"
 
 namespace lowbit {
 
-template <int FMT> struct FmtTraits;
-template <> struct FmtTraits<LB_FMT_INT4> { static constexpr int E = 32; static constexpr int BITS = 4; };
-template <> struct FmtTraits<LB_FMT_NF4> { static constexpr int E = 32; static constexpr int BITS = 4; };
-template <> struct FmtTraits<LB_FMT_INT8> { static constexpr int E = 16; static constexpr int BITS = 8; };
-template <> struct FmtTraits<LB_FMT_FP16> { static constexpr int E = 8; static constexpr int BITS = 16; };
-
 constexpr int kWarps = 8;
 constexpr int kMaxRowGroups = 2;          // 16-row groups per warp
-constexpr int kLutWords = 256 * 32;
+constexpr int kLutWords = 256 * 64;       // NF4 table with a 256-byte entry stride
 constexpr int kMaxGemvCounters = 4096;    // arrival counters available in the workspace
 
 struct GemvParams {
@@ -55,88 +49,6 @@ struct GemvParams {
   int *counters;         // [gridDim.x] arrival counters (zero between calls)
   int prefetch;
 };
-
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// The lane's 16-byte chunk -> its fp16 pairs, in the format's natural unpack order.
-//   INT4: word w -> (e0,e4) (e1,e5) (e2,e6) (e3,e7) of elements 8w..8w+7
-//   NF4 : byte b of word w -> (e2b, e2b+1)
-//   INT8: word w -> (e0,e2) (e1,e3) of elements 4w..4w+3
-//   FP16: natural pairs
-template <int FMT>
-__device__ __forceinline__ void unpack_chunk(const uint4 &q, __half2 s2, bool scale, const uint32_t *lut_lane,
-                                             uint32_t (&p)[FmtTraits<FMT>::E / 2]) {
-  const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-  if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      if constexpr (FMT == LB_FMT_INT4) {
-        uint32_t o[4];
-        int4_word_to_h2(wv[w], o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) p[4 * w + j] = o[j];
-      } else {
-        const uint32_t b = wv[w];
-        p[4 * w + 0] = lut_lane[(b << 5) & 0x1FE0u];
-        p[4 * w + 1] = lut_lane[(b >> 3) & 0x1FE0u];
-        p[4 * w + 2] = lut_lane[(b >> 11) & 0x1FE0u];
-        p[4 * w + 3] = lut_lane[(b >> 19) & 0x1FE0u];
-      }
-    }
-  } else if constexpr (FMT == LB_FMT_INT8) {
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      uint32_t o[2];
-      int8_word_to_h2(wv[w], o);
-      p[2 * w] = o[0];
-      p[2 * w + 1] = o[1];
-    }
-  } else {
-#pragma unroll
-    for (int w = 0; w < 4; ++w) p[w] = wv[w];
-  }
-  if (scale) {
-#pragma unroll
-    for (int i = 0; i < FmtTraits<FMT>::E / 2; ++i) p[i] = h2_as_u32(__hmul2(u32_as_h2(p[i]), s2));  // rn16(code*scale)
-  }
-}
-
-// x pairs for the lane's chunk, permuted to match unpack_chunk's pair order.
-template <int FMT>
-__device__ __forceinline__ void load_x_pairs(const __half *xrow, int chunk, bool valid, uint32_t (&xr)[FmtTraits<FMT>::E / 2]) {
-  constexpr int E = FmtTraits<FMT>::E;
-  uint32_t nat[E / 2];
-#pragma unroll
-  for (int v = 0; v < E / 8; ++v) {
-    const uint4 q = valid ? *reinterpret_cast<const uint4 *>(xrow + size_t(chunk) * E + v * 8) : make_uint4(0, 0, 0, 0);
-    nat[v * 4 + 0] = q.x; nat[v * 4 + 1] = q.y; nat[v * 4 + 2] = q.z; nat[v * 4 + 3] = q.w;
-  }
-  if constexpr (FMT == LB_FMT_INT4) {
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t A = nat[w * 4 + 0], B = nat[w * 4 + 1], C = nat[w * 4 + 2], D = nat[w * 4 + 3];
-      xr[w * 4 + 0] = __byte_perm(A, C, 0x5410);   // (x0, x4)
-      xr[w * 4 + 1] = __byte_perm(A, C, 0x7632);   // (x1, x5)
-      xr[w * 4 + 2] = __byte_perm(B, D, 0x5410);   // (x2, x6)
-      xr[w * 4 + 3] = __byte_perm(B, D, 0x7632);   // (x3, x7)
-    }
-  } else if constexpr (FMT == LB_FMT_INT8) {
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t A = nat[w * 2 + 0], B = nat[w * 2 + 1];
-      xr[w * 2 + 0] = __byte_perm(A, B, 0x5410);   // (x0, x2)
-      xr[w * 2 + 1] = __byte_perm(A, B, 0x7632);   // (x1, x3)
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < E / 2; ++i) xr[i] = nat[i];
-  }
-}
 
 template <int FMT, int NCOL>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
@@ -161,46 +73,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   const int kb0 = blockIdx.y * p.kb_per_split;
   const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
 
-  pdl_launch();
-  if (p.prefetch && threadIdx.x == 0) {
-    // weights never change during the program, so their HBM stream may start before
-    // the predecessor kernel has finished
-    const int rows = min(rows_cta, p.n - row0);
-    const int64_t off = int64_t(kb0) * 64;
-    const int64_t end = int64_t(kb1) * 64 < row_bytes ? int64_t(kb1) * 64 : row_bytes;
-    const int64_t len = end - off;
-    if (len == row_bytes) {
-      const uint8_t *base = p.codes + int64_t(row0) * row_bytes;
-      const int64_t total = int64_t(rows) * row_bytes;
-      for (int64_t o = 0; o < total; o += 65536) prefetch_l2_bulk(base + o, uint32_t(total - o < 65536 ? total - o : 65536));
-    } else if ((len & 15) == 0) {
-      for (int r = 0; r < rows; ++r) prefetch_l2_bulk(p.codes + int64_t(row0 + r) * row_bytes + off, uint32_t(len));
-    }
-  }
-  if constexpr (FMT == LB_FMT_NF4) {
-    fill_nf4_pair_lut(lut);
-    __syncthreads();
-  }
-  pdl_wait();
-
   const int groups_per_row = FMT == LB_FMT_FP16 ? 1 : p.k / p.group;
   const bool per_row_scale = FMT == LB_FMT_INT8 && p.group == p.k;
-  const uint32_t *lut_lane = lut + lane;
-
-  float acc[kMaxRowGroups][NCOL][4];
-#pragma unroll
-  for (int r = 0; r < kMaxRowGroups; ++r)
-#pragma unroll
-    for (int c = 0; c < NCOL; ++c)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[r][c][i] = 0.f;
-
-  // Two K blocks per round: every weight load of the round is in flight before the
-  // first dequant, so each warp pays the memory latency once per round.
-  for (int kbA = kb0 + kw; kbA < kb1; kbA += 2 * p.warps_k) {
-    uint4 q[2][kMaxRowGroups][2];
-    __half2 s2[2][kMaxRowGroups][2];
-    uint32_t xr[2][NCOL][NP];
+  // One round of weight loads: two K blocks x rpw row groups x rows g / g+8, with scales.
+  auto load_round = [&](int kbA, uint4 (&q)[2][kMaxRowGroups][2], __half2 (&s2)[2][kMaxRowGroups][2]) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int kb = kbA + u * p.warps_k;
@@ -222,6 +98,57 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
           }
         }
       }
+    }
+  };
+  // Weights and scales never change while the program runs, so the first round is
+  // requested before waiting on the predecessor kernel (bit 1 of p.prefetch).
+  const int kb_first = kb0 + kw;
+  const bool preloaded = (p.prefetch & 2) && kb_first < kb1;
+  uint4 q_first[2][kMaxRowGroups][2];
+  __half2 s_first[2][kMaxRowGroups][2];
+  if (preloaded) load_round(kb_first, q_first, s_first);
+
+  pdl_launch();
+  if ((p.prefetch & 1) && warp == 0) {
+    // the rest of the CTA's weight bytes (K blocks past its first round) start moving
+    // into L2 as well; lane r covers rows r, r + 32, ...
+    const int rows = min(rows_cta, p.n - row0);
+    const int kb_rest = (p.prefetch & 2) ? kb0 + 2 * p.warps_k : kb0;
+    const int64_t off = int64_t(kb_rest) * 64;
+    const int64_t end = int64_t(kb1) * 64 < row_bytes ? int64_t(kb1) * 64 : row_bytes;
+    if (end > off && ((end - off) & 15) == 0)
+      for (int r = lane; r < rows; r += 32)
+        prefetch_l2_bulk(p.codes + int64_t(row0 + r) * row_bytes + off, uint32_t(end - off));
+  }
+  if constexpr (FMT == LB_FMT_NF4) {
+    fill_nf4_pair_lut<64>(lut);
+    __syncthreads();
+  }
+  pdl_wait();
+
+  const char *lutb = reinterpret_cast<const char *>(lut);
+  const uint32_t lane4 = uint32_t(lane) * 4u;
+
+  // two accumulator chains per (row group, column): consecutive MMA tiles alternate, so
+  // each waits on the one two tiles back
+  float acc[kMaxRowGroups][NCOL][2][4];
+#pragma unroll
+  for (int r = 0; r < kMaxRowGroups; ++r)
+#pragma unroll
+    for (int c = 0; c < NCOL; ++c)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[r][c][h][i] = 0.f;
+
+  // x pairs of a round, then dequant + MMA of its weights.
+  auto compute_round = [&](int kbA, const uint4 (&q)[2][kMaxRowGroups][2], const __half2 (&s2)[2][kMaxRowGroups][2]) {
+    uint32_t xr[2][NCOL][NP];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int kb = kbA + u * p.warps_k;
+      const int chunk = kb * 4 + t;
+      const bool kvalid = kb < kb1 && chunk < chunks;
 #pragma unroll
       for (int c = 0; c < NCOL; ++c)
         load_x_pairs<FMT>(p.x + size_t(g + 8 * c) * p.k, chunk, kvalid && g + 8 * c < p.m, xr[u][c]);
@@ -233,16 +160,26 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       for (int r = 0; r < kMaxRowGroups; ++r) {
         if (r >= p.rpw) break;
         uint32_t a0[NP], a1[NP];
-        unpack_chunk<FMT>(q[u][r][0], s2[u][r][0], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lut_lane, a0);
-        unpack_chunk<FMT>(q[u][r][1], s2[u][r][1], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lut_lane, a1);
+        unpack_chunk<FMT>(q[u][r][0], s2[u][r][0], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lutb, lane4, a0);
+        unpack_chunk<FMT>(q[u][r][1], s2[u][r][1], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lutb, lane4, a1);
 #pragma unroll
         for (int j = 0; j < TILES; ++j) {
           const uint32_t a[4] = {a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1]};
 #pragma unroll
-          for (int c = 0; c < NCOL; ++c) mma16816(acc[r][c], a, xr[u][c][2 * j], xr[u][c][2 * j + 1]);
+          for (int c = 0; c < NCOL; ++c) mma16816(acc[r][c][j & 1], a, xr[u][c][2 * j], xr[u][c][2 * j + 1]);
         }
       }
     }
+  };
+
+  // Two K blocks per round: every weight load of the round is in flight before the
+  // first dequant, so each warp pays the memory latency once per round.
+  if (preloaded) compute_round(kb_first, q_first, s_first);
+  for (int kbA = preloaded ? kb_first + 2 * p.warps_k : kb_first; kbA < kb1; kbA += 2 * p.warps_k) {
+    uint4 q[2][kMaxRowGroups][2];
+    __half2 s2[2][kMaxRowGroups][2];
+    load_round(kbA, q, s2);
+    compute_round(kbA, q, s2);
   }
 
   // C fragment: acc[r][c] = {C[g][2t], C[g][2t+1], C[g+8][2t], C[g+8][2t+1]} with rows =
@@ -253,10 +190,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
 #pragma unroll
     for (int c = 0; c < NCOL; ++c) {
       float *base = red + (kw * rows_cta + 16 * (p.rpw * rw + r)) * 16 + 8 * c + 2 * t;
-      base[g * 16] = acc[r][c][0];
-      base[g * 16 + 1] = acc[r][c][1];
-      base[(g + 8) * 16] = acc[r][c][2];
-      base[(g + 8) * 16 + 1] = acc[r][c][3];
+      base[g * 16] = acc[r][c][0][0] + acc[r][c][1][0];
+      base[g * 16 + 1] = acc[r][c][0][1] + acc[r][c][1][1];
+      base[(g + 8) * 16] = acc[r][c][0][2] + acc[r][c][1][2];
+      base[(g + 8) * 16 + 1] = acc[r][c][0][3] + acc[r][c][1][3];
     }
   }
   __syncthreads();
@@ -425,11 +362,14 @@ bool gemv_supported(int fmt, int group, int m, int n, int k) {
   return true;
 }
 
-static int prefetch_mode() {
+// bit 0: L2 prefetch of the CTA's weight bytes past its first round, bit 1: first round
+// of weight loads into registers, both before waiting on the predecessor
+// (LOWBIT_GEMV_PREFETCH, default 3).
+int gemv_prefetch_mode() {
   static int v = -1;
   if (v < 0) {
     const char *s = getenv("LOWBIT_GEMV_PREFETCH");
-    v = (s && s[0] == '0') ? 0 : 1;
+    v = s ? (atoi(s) & 3) : 3;
   }
   return v;
 }
@@ -530,7 +470,7 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
     p.partial = static_cast<float *>(scratch);
     p.counters = counters;
   }
-  p.prefetch = prefetch_mode();
+  p.prefetch = gemv_prefetch_mode();
   const int ncol = m <= 8 ? 1 : 2;
   size_t smem = size_t(kWarps) * 64 * 16 * sizeof(float);
   if (fmt == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
