@@ -198,9 +198,10 @@ def dominant_kernel_roofline(device, stream, peak_gbs):
             'traffic': TRAFFIC_PER_LAUNCH.get(DOMINANT)}
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel, from
-# the committed ncu capture (profiles/gemv_nf4_g64_8192x2048_m1.md); None until captured.
-TRAFFIC_PER_LAUNCH = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel (mean of
+# the two captured launches), from the committed ncu capture
+# (profiles/gemv_nf4_g64_8192x2048_m1.md).
+TRAFFIC_PER_LAUNCH = {DOMINANT: 8976256}
 
 
 def cpu_reference_sweep(sample_cells, reps):
@@ -444,6 +445,36 @@ def run_reference(args):
     return 0
 
 
+def profile_case(which):
+    """Small, self-contained workloads for ncu captures (committed so that the profile
+    commands in profiles/ run committed files only).  dominant: the NF4 g64 8192x2048
+    decode GEMV (M=1) over 16 weight replicas (144 MB, larger than L2), 48 launches;
+    prefill: the same layer at M=2048 with the rank-32 correction on the tensor-core
+    path, 6 launches."""
+    import lowbit_runtime as rt
+    rt.require_cuda()
+    fmt, g, n, k = DOMINANT
+    gen = torch.Generator(device='cpu').manual_seed(3)
+    reps = 16 if which == 'dominant' else 2
+    packed = [rt.quantize_pack((torch.randn(n, k, generator=gen) * 0.02).half().cuda(), fmt, g) for _ in range(reps)]
+    m = 1 if which == 'dominant' else 2048
+    x = torch.randn(m, k, generator=gen).half().cuda()
+    v = (torch.randn(RANK, k, generator=gen) * 1e-3).half().cuda()
+    u = (torch.randn(n, RANK, generator=gen) * 1e-3).half().cuda()
+    y = torch.empty(m, n, dtype=torch.float16, device='cuda')
+    launches = 48 if which == 'dominant' else 6
+    for i in range(launches):
+        c, sc = packed[i % reps]
+        if which == 'dominant':
+            rt.linear(x, fmt, g, n, c, sc, out=y)
+        else:
+            rt.linear(x, fmt, g, n, c, sc, down=v, up=u, out=y)
+    torch.cuda.synchronize()
+    print(json.dumps({'profile_case': which, 'launches': launches, 'm': m, 'n': n, 'k': k, 'format': fmt,
+                      'group': g, 'checksum': float(y.float().abs().sum())}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -453,7 +484,11 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decode', action='store_true')
     ap.add_argument('--quick-decode', action='store_true')
+    ap.add_argument('--profile', choices=['dominant', 'prefill'],
+                    help='run a small fixed workload for an ncu capture and exit')
     args = ap.parse_args()
+    if args.profile:
+        return profile_case(args.profile)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == 'reference':

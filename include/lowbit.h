@@ -112,7 +112,7 @@ int lb_linear_select(int fmt, int group, int m, int n, int k, int rank);
  * For callers that cannot provide a workspace -- a host application linking this
  * library whose device memory belongs to an allocator it may not call, or a
  * latency-critical thread where a first cudaMalloc would block -- this is lb_linear
- * restricted to the decode GEMV (M <= 16, 16-byte aligned x / codes / y / factors).
+ * restricted to the decode GEMV (M <= 64, 16-byte aligned x / codes / y / factors).
  * Its scratch (correction projection, split-K partials, arrival counters) is one fixed
  * array of LB_NOALLOC_SCRATCH_BYTES compiled into the library; every GPU that loads the
  * library holds it until the process exits.  The call allocates nothing; the caller

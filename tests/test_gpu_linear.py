@@ -111,7 +111,7 @@ CASES = [
 
 
 @pytest.mark.parametrize('n,k,fmt,g', CASES)
-@pytest.mark.parametrize('m', [1, 2, 3, 4, 16, 100, 256])
+@pytest.mark.parametrize('m', [1, 2, 3, 4, 16, 24, 40, 64, 100, 256])
 def test_linear_matches_oracle_with_correction(rt, n, k, fmt, g, m):
     w, u, v = baseline_weight(n, k, seed=n + k)
     group, data, scales = ref.quantize(w.numpy(), fmt, g)
@@ -167,7 +167,8 @@ def test_ragged_shapes_and_ranks(rt, n, k, fmt, g, rank):
 
 
 @pytest.mark.parametrize('plan', ['1,1,1', '2,4,1', '8,2,1', '8,1,4', '4,2,2', '1,4,8'])
-@pytest.mark.parametrize('fmt,g,m', [('nf4', 64, 1), ('int4', 128, 5), ('int8', 2048, 16), ('int8', 64, 3)])
+@pytest.mark.parametrize('fmt,g,m', [('nf4', 64, 1), ('int4', 128, 5), ('int8', 2048, 16), ('int8', 64, 3),
+                                     ('nf4', 128, 37), ('int4', 64, 64)])
 def test_gemv_work_splits_agree(rt, monkeypatch, plan, fmt, g, m):
     """Every GEMV work split (warps over K, rows per warp, cross-CTA K splits with the
     workspace reduction) gives the same parity; cross-CTA splits are deterministic."""

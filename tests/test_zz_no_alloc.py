@@ -70,9 +70,9 @@ def test_noalloc_rejects_what_it_cannot_hold(monkeypatch):
     import lowbit_runtime as rt
     rt.require_cuda()
     group, codes, sc, u, v = _weights(1024, 2048, 'nf4', 64, seed=1)
-    x = torch.randn(32, 2048).half().cuda()
-    y = torch.empty(32, 1024, dtype=torch.float16, device='cuda')
-    assert _noalloc(rt, 'nf4', group, x, 1024, codes, sc, v, u, y) == rt.UNSUPPORTED   # M > 16 is not the GEMV
+    x = torch.randn(65, 2048).half().cuda()
+    y = torch.empty(65, 1024, dtype=torch.float16, device='cuda')
+    assert _noalloc(rt, 'nf4', group, x, 1024, codes, sc, v, u, y) == rt.UNSUPPORTED   # M > 64 is not the GEMV
     monkeypatch.setenv('LOWBIT_GEMV_PLAN', '8,1,8')
     m, n, k = 16, 32768, 4096                                   # partials: 8 x 16 x 32768 fp32 = 16 MiB
     x = torch.randn(m, k).half().cuda()

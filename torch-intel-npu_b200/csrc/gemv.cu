@@ -1,4 +1,4 @@
-// K2: decode dequant-GEMV for M <= 16 with the rank-r correction in the epilogue.
+// K2: decode dequant-GEMV for M <= 64 with the rank-r correction in the epilogue.
 //
 // HBM-bound by design.  Each warp streams 16-row weight groups: lane (g, t) = (lane/4,
 // lane%4) issues one 128-bit coalesced load of row g and one of row g+8 per 64-byte
@@ -50,14 +50,22 @@ struct GemvParams {
   int prefetch;
 };
 
+// NCOL = 8-column groups of activation rows (M <= 8 NCOL).  Up to 16 columns the x pairs
+// of a round are loaded up front and each warp may hold two row groups with two
+// accumulator chains; from 32 columns on (batched decode) a warp holds one row group and
+// its dequantized fragments are reused across the column groups while x is streamed.
 template <int FMT, int NCOL>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   constexpr int E = FmtTraits<FMT>::E;
   constexpr int NP = E / 2;          // pairs per lane chunk
   constexpr int TILES = NP / 2;      // m16n8k16 tiles per K block
   constexpr bool kScaled4 = FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4;
+  constexpr bool kWide = NCOL > 2;
+  constexpr int RG = kWide ? 1 : kMaxRowGroups;   // row groups a warp can hold
+  constexpr int CH = kWide ? 1 : 2;               // accumulator chains per (row group, column group)
+  constexpr int LDC = 8 * NCOL;                   // reduction row stride (columns)
   extern __shared__ __align__(16) uint32_t smem[];
-  float *red = reinterpret_cast<float *>(smem);                        // [warps_k][rows_cta][16 m]
+  float *red = reinterpret_cast<float *>(smem);                        // [warps_k][rows_cta][LDC]
   uint32_t *lut = smem + kWarps * 64 * 16;
   __shared__ int s_last;
 
@@ -76,14 +84,14 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   const int groups_per_row = FMT == LB_FMT_FP16 ? 1 : p.k / p.group;
   const bool per_row_scale = FMT == LB_FMT_INT8 && p.group == p.k;
   // One round of weight loads: two K blocks x rpw row groups x rows g / g+8, with scales.
-  auto load_round = [&](int kbA, uint4 (&q)[2][kMaxRowGroups][2], __half2 (&s2)[2][kMaxRowGroups][2]) {
+  auto load_round = [&](int kbA, uint4 (&q)[2][RG][2], __half2 (&s2)[2][RG][2]) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int kb = kbA + u * p.warps_k;
       const int chunk = kb * 4 + t;
       const bool kvalid = kb < kb1 && chunk < chunks;
 #pragma unroll
-      for (int r = 0; r < kMaxRowGroups; ++r) {
+      for (int r = 0; r < RG; ++r) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int row = wrow0 + 16 * r + g + 8 * h;
@@ -104,8 +112,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   // requested before waiting on the predecessor kernel (bit 1 of p.prefetch).
   const int kb_first = kb0 + kw;
   const bool preloaded = (p.prefetch & 2) && kb_first < kb1;
-  uint4 q_first[2][kMaxRowGroups][2];
-  __half2 s_first[2][kMaxRowGroups][2];
+  uint4 q_first[2][RG][2];
+  __half2 s_first[2][RG][2];
   if (preloaded) load_round(kb_first, q_first, s_first);
 
   pdl_launch();
@@ -131,42 +139,68 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
 
   // two accumulator chains per (row group, column): consecutive MMA tiles alternate, so
   // each waits on the one two tiles back
-  float acc[kMaxRowGroups][NCOL][2][4];
+  float acc[RG][NCOL][CH][4];
 #pragma unroll
-  for (int r = 0; r < kMaxRowGroups; ++r)
+  for (int r = 0; r < RG; ++r)
 #pragma unroll
     for (int c = 0; c < NCOL; ++c)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < CH; ++h)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[r][c][h][i] = 0.f;
 
   // x pairs of a round, then dequant + MMA of its weights.
-  auto compute_round = [&](int kbA, const uint4 (&q)[2][kMaxRowGroups][2], const __half2 (&s2)[2][kMaxRowGroups][2]) {
-    uint32_t xr[2][NCOL][NP];
+  auto compute_round = [&](int kbA, const uint4 (&q)[2][RG][2], const __half2 (&s2)[2][RG][2]) {
+    const bool scale = kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale);
+    if constexpr (!kWide) {
+      uint32_t xr[2][NCOL][NP];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int kb = kbA + u * p.warps_k;
-      const int chunk = kb * 4 + t;
-      const bool kvalid = kb < kb1 && chunk < chunks;
+      for (int u = 0; u < 2; ++u) {
+        const int kb = kbA + u * p.warps_k;
+        const int chunk = kb * 4 + t;
+        const bool kvalid = kb < kb1 && chunk < chunks;
 #pragma unroll
-      for (int c = 0; c < NCOL; ++c)
-        load_x_pairs<FMT>(p.x + size_t(g + 8 * c) * p.k, chunk, kvalid && g + 8 * c < p.m, xr[u][c]);
-    }
+        for (int c = 0; c < NCOL; ++c)
+          load_x_pairs<FMT>(p.x + size_t(g + 8 * c) * p.k, chunk, kvalid && g + 8 * c < p.m, xr[u][c]);
+      }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (u == 1 && kbA + p.warps_k >= kb1) break;
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && kbA + p.warps_k >= kb1) break;
 #pragma unroll
-      for (int r = 0; r < kMaxRowGroups; ++r) {
-        if (r >= p.rpw) break;
+        for (int r = 0; r < RG; ++r) {
+          if (r >= p.rpw) break;
+          uint32_t a0[NP], a1[NP];
+          unpack_chunk<FMT>(q[u][r][0], s2[u][r][0], scale, lutb, lane4, a0);
+          unpack_chunk<FMT>(q[u][r][1], s2[u][r][1], scale, lutb, lane4, a1);
+#pragma unroll
+          for (int j = 0; j < TILES; ++j) {
+            const uint32_t a[4] = {a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1]};
+#pragma unroll
+            for (int c = 0; c < NCOL; ++c) mma16816(acc[r][c][j % CH], a, xr[u][c][2 * j], xr[u][c][2 * j + 1]);
+          }
+        }
+      }
+    } else {
+      // one row group: its dequantized fragments serve every column group in turn
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && kbA + p.warps_k >= kb1) break;
+        const int kb = kbA + u * p.warps_k;
+        const int chunk = kb * 4 + t;
+        const bool kvalid = kb < kb1 && chunk < chunks;
         uint32_t a0[NP], a1[NP];
-        unpack_chunk<FMT>(q[u][r][0], s2[u][r][0], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lutb, lane4, a0);
-        unpack_chunk<FMT>(q[u][r][1], s2[u][r][1], kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale), lutb, lane4, a1);
+        unpack_chunk<FMT>(q[u][0][0], s2[u][0][0], scale, lutb, lane4, a0);
+        unpack_chunk<FMT>(q[u][0][1], s2[u][0][1], scale, lutb, lane4, a1);
 #pragma unroll
-        for (int j = 0; j < TILES; ++j) {
-          const uint32_t a[4] = {a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1]};
+        for (int c = 0; c < NCOL; ++c) {
+          if (8 * c >= p.m) break;   // column groups past the activation rows
+          uint32_t xr[NP];
+          load_x_pairs<FMT>(p.x + size_t(g + 8 * c) * p.k, chunk, kvalid && g + 8 * c < p.m, xr);
 #pragma unroll
-          for (int c = 0; c < NCOL; ++c) mma16816(acc[r][c][j & 1], a, xr[u][c][2 * j], xr[u][c][2 * j + 1]);
+          for (int j = 0; j < TILES; ++j) {
+            const uint32_t a[4] = {a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1]};
+            mma16816(acc[0][c][0], a, xr[2 * j], xr[2 * j + 1]);
+          }
         }
       }
     }
@@ -176,8 +210,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   // first dequant, so each warp pays the memory latency once per round.
   if (preloaded) compute_round(kb_first, q_first, s_first);
   for (int kbA = preloaded ? kb_first + 2 * p.warps_k : kb_first; kbA < kb1; kbA += 2 * p.warps_k) {
-    uint4 q[2][kMaxRowGroups][2];
-    __half2 s2[2][kMaxRowGroups][2];
+    uint4 q[2][RG][2];
+    __half2 s2[2][RG][2];
     load_round(kbA, q, s2);
     compute_round(kbA, q, s2);
   }
@@ -185,15 +219,22 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   // C fragment: acc[r][c] = {C[g][2t], C[g][2t+1], C[g+8][2t], C[g+8][2t+1]} with rows =
   // weight rows 16r + {g, g+8}, columns = activation rows 8c + {2t, 2t+1}
 #pragma unroll
-  for (int r = 0; r < kMaxRowGroups; ++r) {
+  for (int r = 0; r < RG; ++r) {
     if (r >= p.rpw) break;
 #pragma unroll
     for (int c = 0; c < NCOL; ++c) {
-      float *base = red + (kw * rows_cta + 16 * (p.rpw * rw + r)) * 16 + 8 * c + 2 * t;
-      base[g * 16] = acc[r][c][0][0] + acc[r][c][1][0];
-      base[g * 16 + 1] = acc[r][c][0][1] + acc[r][c][1][1];
-      base[(g + 8) * 16] = acc[r][c][0][2] + acc[r][c][1][2];
-      base[(g + 8) * 16 + 1] = acc[r][c][0][3] + acc[r][c][1][3];
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[i] = acc[r][c][0][i];
+#pragma unroll
+        for (int h = 1; h < CH; ++h) v[i] += acc[r][c][h][i];
+      }
+      float *base = red + (kw * rows_cta + 16 * (p.rpw * rw + r)) * LDC + 8 * c + 2 * t;
+      base[g * LDC] = v[0];
+      base[g * LDC + 1] = v[1];
+      base[(g + 8) * LDC] = v[2];
+      base[(g + 8) * LDC + 1] = v[3];
     }
   }
   __syncthreads();
@@ -206,7 +247,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
       if (n >= p.n) continue;
       float v = 0.f;
-      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * 16 + mm];
+      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * LDC + mm];
       p.partial[blockIdx.y * mn + int64_t(mm) * p.n + n] = v;
     }
     __threadfence();
@@ -220,30 +261,85 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       if (n >= p.n) continue;
       float v = 0.f;
       for (int sp = 0; sp < splits; ++sp) v += __ldcg(p.partial + sp * mn + int64_t(mm) * p.n + n);
-      red[rl * 16 + mm] = v;   // warp-0 slot reused for the total
+      red[rl * LDC + mm] = v;   // warp-0 slot reused for the total
     }
     if (threadIdx.x == 0) p.counters[blockIdx.x] = 0;   // ready for the next call
     __syncthreads();
   }
 
-  for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
-    const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
-    if (n >= p.n) continue;
-    float v = 0.f;
-    if (splits > 1) v = red[rl * 16 + mm];
-    else
-      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * 16 + mm];
-    if (per_row_scale) v *= __half2float(p.scales[n]);
-    __half yq = __float2half_rn(v);
-    if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
-    if (p.z) {
-      const __half *zr = p.z + mm * 32;
-      const __half *ur = p.up + int64_t(n) * p.rank;
-      float d = 0.f;
-      for (int r = 0; r < p.rank; ++r) d = fmaf(__half2float(zr[r]), __half2float(ur[r]), d);
-      yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(d)));
+  // Totals into the warp-0 slot (each thread owns its (row, column) entries).
+  if (splits == 1 && p.warps_k > 1) {
+    for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+      const int mm = idx / rows_cta, rl = idx % rows_cta;
+      float v = 0.f;
+      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * LDC + mm];
+      red[rl * LDC + mm] = v;
     }
-    p.y[int64_t(mm) * p.n + n] = yq;
+    __syncthreads();
+  }
+
+  if (!p.z) {
+    for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+      const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+      if (n >= p.n) continue;
+      float v = red[rl * LDC + mm];
+      if (per_row_scale) v *= __half2float(p.scales[n]);
+      __half yq = __float2half_rn(v);
+      if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
+      p.y[int64_t(mm) * p.n + n] = yq;
+    }
+    return;
+  }
+
+  // Correction delta = half(z . U[n]^T) on the tensor cores: per 16-row group, U rows
+  // (rank padded to 32 with zeros) are the A operand and z (zero beyond the rank) the
+  // B operand, two m16n8k16 tiles per 8-column group; then
+  // y = half(half(half(acc) + bias) + delta) as torch_npu_smollm.py:150-164 stages it.
+  for (int rg = warp; rg < rows_cta / 16; rg += kWarps) {
+    const int rl0 = rg * 16;
+    uint32_t ua[2][4];
+#pragma unroll
+    for (int kt = 0; kt < 2; ++kt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = row0 + rl0 + g + 8 * (i & 1);
+        const int kk = 16 * kt + 2 * t + 8 * (i >> 1);
+        __half lo = __float2half(0.f), hi = lo;
+        if (row < p.n) {
+          const __half *ur = p.up + int64_t(row) * p.rank;
+          if (kk < p.rank) lo = ur[kk];
+          if (kk + 1 < p.rank) hi = ur[kk + 1];
+        }
+        ua[kt][i] = h2_as_u32(__halves2half2(lo, hi));
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < NCOL; ++c) {
+      if (8 * c >= p.m) break;
+      const int mz = 8 * c + g;   // activation row of this lane's B column
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kt = 0; kt < 2; ++kt) {
+        uint32_t b0 = 0, b1 = 0;
+        if (mz < p.m) {
+          const uint32_t *zr = reinterpret_cast<const uint32_t *>(p.z + mz * 32);
+          b0 = zr[8 * kt + t];
+          b1 = zr[8 * kt + t + 4];
+        }
+        mma16816(d, ua[kt], b0, b1);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rl = rl0 + g + 8 * (i >> 1), mm = 8 * c + 2 * t + (i & 1), n = row0 + rl;
+        if (n >= p.n || mm >= p.m) continue;
+        float v = red[rl * LDC + mm];
+        if (per_row_scale) v *= __half2float(p.scales[n]);
+        __half yq = __float2half_rn(v);
+        if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
+        yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(d[i])));
+        p.y[int64_t(mm) * p.n + n] = yq;
+      }
+    }
   }
 }
 
@@ -354,9 +450,12 @@ using namespace lowbit;
 
 int gemv_elems(int fmt) { return fmt == LB_FMT_INT8 ? 16 : (fmt == LB_FMT_FP16 ? 8 : 32); }
 
+// Decode batches up to 64 activation rows: per 16 weight rows the MMA work grows with M,
+// but the weights are still read and dequantized once, which the tcgen05 path (one
+// 128-row weight tile per CTA regardless of M) cannot match at these sizes.
 bool gemv_supported(int fmt, int group, int m, int n, int k) {
   const int e = gemv_elems(fmt);
-  if (m < 1 || m > 16 || n < 1 || k < e || k % e) return false;
+  if (m < 1 || m > 64 || n < 1 || k < e || k % e) return false;
   if (fmt != LB_FMT_FP16 && fmt != LB_FMT_INT8 && group % e) return false;
   if (fmt == LB_FMT_INT8 && group != k && group % e) return false;
   return true;
@@ -380,7 +479,7 @@ struct GemvPlan { int warps_k, rpw, splits, kb_per_split, ctas_x; };
 // (2 per SM) must keep ~6 MB of 128-bit loads in flight to cover HBM latency, every
 // extra wave repeats the latency, and a cross-CTA K split adds a reduction pass.
 // LOWBIT_GEMV_PLAN="warps_k,rpw,splits" overrides the choice (tuning).
-static GemvPlan gemv_plan(int fmt, int n, int k) {
+static GemvPlan gemv_plan(int fmt, int m, int n, int k) {
   const int e = gemv_elems(fmt);
   const int kblocks = (k / e + 3) / 4;
   const int groups = (n + 15) / 16;
@@ -390,7 +489,7 @@ static GemvPlan gemv_plan(int fmt, int n, int k) {
   GemvPlan best = {1, 1, 1, kblocks, groups};
   double best_cost = 1e30;
   for (int wk = 1; wk <= kWarps; wk *= 2) {
-    for (int rpw = 1; rpw <= kMaxRowGroups; rpw *= 2) {
+    for (int rpw = 1; rpw <= (m > 16 ? 1 : kMaxRowGroups); rpw *= 2) {
       for (int sp = 1; sp <= 16; sp *= 2) {
         if (fwk && (wk != fwk || rpw != frpw || sp != fsp)) continue;
         if (sp > 1 && ((groups + (kWarps / wk) * rpw - 1) / ((kWarps / wk) * rpw)) > kMaxGemvCounters) continue;
@@ -405,7 +504,7 @@ static GemvPlan gemv_plan(int fmt, int n, int k) {
         const double fill = resident * kWarps * loads * 1024.0 / 6.0e6;
         const int waves = (ctas + 2 * 148 - 1) / (2 * 148);
         double cost = waves * (0.6 * rounds + 0.4 + 0.05 * loads) / (fill < 1.0 ? fill : 1.0);
-        if (sp > 1) cost += 0.5;
+        if (sp > 1) cost += 0.5 + (m > 16 ? m / 16.0 : 0.0);   // the last CTA's partial sums grow with M
         if (cost < best_cost) { best_cost = cost; best = {wk, rpw, (kblocks + kbs - 1) / kbs, kbs, (groups + wr * rpw - 1) / (wr * rpw)}; }
       }
     }
@@ -414,7 +513,7 @@ static GemvPlan gemv_plan(int fmt, int n, int k) {
 }
 
 size_t gemv_workspace_bytes(int fmt, int m, int n, int k) {
-  const GemvPlan pl = gemv_plan(fmt, n, k);
+  const GemvPlan pl = gemv_plan(fmt, m, n, k);
   if (pl.splits <= 1) return 0;
   return size_t(pl.splits) * m * n * sizeof(float);
 }
@@ -429,7 +528,12 @@ static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t smem, cu
 
 template <int FMT>
 static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_t smem, cudaStream_t st) {
-  return ncol == 1 ? launch_gemv_t<FMT, 1>(p, grid, smem, st) : launch_gemv_t<FMT, 2>(p, grid, smem, st);
+  switch (ncol) {
+    case 1: return launch_gemv_t<FMT, 1>(p, grid, smem, st);
+    case 2: return launch_gemv_t<FMT, 2>(p, grid, smem, st);
+    case 4: return launch_gemv_t<FMT, 4>(p, grid, smem, st);
+    default: return launch_gemv_t<FMT, 8>(p, grid, smem, st);
+  }
 }
 
 cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, const uint16_t *v, uint16_t *z,
@@ -461,7 +565,7 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   p.rank = rank;
   p.bias = reinterpret_cast<const __half *>(bias);
   p.y = reinterpret_cast<__half *>(y);
-  const GemvPlan pl = gemv_plan(fmt, n, k);
+  const GemvPlan pl = gemv_plan(fmt, m, n, k);
   p.warps_k = pl.warps_k;
   p.rpw = pl.rpw;
   p.kblocks = (k / gemv_elems(fmt) + 3) / 4;
@@ -471,7 +575,7 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
     p.counters = counters;
   }
   p.prefetch = gemv_prefetch_mode();
-  const int ncol = m <= 8 ? 1 : 2;
+  const int ncol = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
   size_t smem = size_t(kWarps) * 64 * 16 * sizeof(float);
   if (fmt == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
   const dim3 grid(pl.ctas_x, pl.splits);

@@ -4,7 +4,7 @@
 // links liblowbit through the C ABI with a device-memory budget owned by another
 // allocator it may not call into, or code on a latency-critical thread where a first
 // cudaMalloc would block and synchronise the device.  For them this entry point runs
-// the decode GEMV (M <= 16) with its scratch -- the correction projection z, split-K
+// the decode GEMV (M <= 64) with its scratch -- the correction projection z, split-K
 // fp32 partials and arrival counters -- in one fixed array compiled into the library,
 // so a call allocates nothing.
 //
@@ -74,7 +74,7 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
   if (!down) rank = 0;
   if (!gemv_supported(fmt, group, m, n, k) || !aligned16(x) || !aligned16(codes) || !aligned16(y) ||
       (down && (!aligned16(down) || !aligned16(up))))
-    return LB_ERR_UNSUPPORTED;   // only the decode GEMV (M <= 16, aligned rows) has this variant
+    return LB_ERR_UNSUPPORTED;   // only the decode GEMV (M <= 64, aligned rows) has this variant
   if (size_t(m) * 32 * 2 > kZBytes ||
       gemv_workspace_bytes(fmt, m, n, k) > size_t(LB_NOALLOC_SCRATCH_BYTES) - kPartialOffset)
     return LB_ERR_WORKSPACE;     // the problem needs more scratch than the fixed array holds
