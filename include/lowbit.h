@@ -105,6 +105,22 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
 /* Which kernel family lb_linear would choose for this problem (enum lb_path). */
 int lb_linear_select(int fmt, int group, int m, int n, int k, int rank);
 
+/* Several linears that read the same activations, as one decode GEMV launch (M <= 64).
+ * No reference counterpart: the reference runs q/k/v (and gate/up) as separate
+ * QuantizedLinear calls (torch_npu_smollm.py:170-173, :187-188).  The caller stacks the
+ * packed rows (codes, scales, bias) of the linears, which must share format and group,
+ * and their corrections as one block-diagonal correction of the summed rank (<= 128):
+ * down = [V_1; V_2; ...] ([rank, K]), up [N, rank] with each linear's U in its own
+ * column block and zeros elsewhere, so every output equals the separate call's
+ * staging exactly.  residual (optional, [M, N]) is added last, y = half(y + residual):
+ * the residual add of torch_npu_smollm.py:192 fused into the down projection.
+ * Workspace: lb_linear_workspace_bytes(fmt, group, m, n, k, rank).  LB_ERR_UNSUPPORTED
+ * when the problem is not a decode GEMV (M > 64, unaligned rows or pointers). */
+int lb_linear_stacked(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                      const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
+                      const uint16_t *bias, const uint16_t *residual, uint16_t *y, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
 /*
  * Allocation-free decode GEMV.  No counterpart in the reference (its linear runs inside
  * an NPU graph session that owns all of its buffers).

@@ -73,7 +73,8 @@ def test_path_selection():
     assert rt.linear_select('nf4', 64, 1, 8192, 2048) == 'gemv'
     assert rt.linear_select('int4', 128, 4, 2048, 8192) == 'gemv'
     assert rt.linear_select('nf4', 64, 16, 8192, 2048) == 'gemv'
-    assert rt.linear_select('nf4', 64, 17, 8192, 2048) == 'tc'
+    assert rt.linear_select('nf4', 64, 64, 8192, 2048) == 'gemv'     # batched decode stays on the GEMV
+    assert rt.linear_select('nf4', 64, 65, 8192, 2048) == 'tc'
     assert rt.linear_select('int8', 576, 128, 1536, 576) == 'tc'
     assert rt.linear_select('int4', 3, 1, 5, 9) == 'generic'      # odd shapes / groups
     assert rt.linear_select('nf4', 64, 128, 8192, 2048, 32) == 'tc'

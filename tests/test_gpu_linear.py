@@ -228,3 +228,41 @@ def test_quantized_linear_module(rt):
         q(x.cuda()[:, :100])
     with pytest.raises(NotImplementedError):
         lb.QuantizedLinear(q.weight, compact_groups=True)
+
+
+@pytest.mark.parametrize('fmt,g', [('nf4', 64), ('int4', 32), ('int8', 576)])
+@pytest.mark.parametrize('m', [1, 5, 64])
+def test_stacked_linear_matches_separate_projections(rt, fmt, g, m):
+    """lb_linear_stacked over q/k/v-shaped rows with their three rank-32 corrections as one
+    block-diagonal rank-96 correction, and the fused residual add: every output row matches
+    the oracle of its own projection, staged as the reference stages it."""
+    k = 576
+    widths = (576, 192, 192)
+    gen = torch.Generator().manual_seed(31 + m)
+    parts = []
+    for n in widths:
+        w = (torch.randn(n, k, generator=gen) * 0.02).half()
+        v = (torch.randn(32, k, generator=gen) * 1e-3).half()
+        u = (torch.randn(n, 32, generator=gen) * 1e-3).half()
+        group, data, scales = ref.quantize(w.numpy(), fmt, g)
+        parts.append((n, group, data, scales, v, u))
+    x = torch.randn(m, k, generator=gen).half()
+    ntot = sum(widths)
+    codes = torch.frombuffer(bytearray(b''.join(p[2] for p in parts)), dtype=torch.uint8).cuda()
+    scales = torch.frombuffer(bytearray(b''.join(p[3] for p in parts)), dtype=torch.float16).cuda()
+    down = torch.zeros(96, k, dtype=torch.float16)
+    up = torch.zeros(ntot, 96, dtype=torch.float16)
+    row = 0
+    for i, (n, _, _, _, v, u) in enumerate(parts):
+        down[32 * i:32 * i + 32] = v
+        up[row:row + n, 32 * i:32 * i + 32] = u
+        row += n
+    group = parts[0][1]
+    expected = torch.cat([_oracle(x, (n, k), fmt, group, data, sc, down=v, up=u) for n, _, data, sc, v, u in parts], 1)
+    y = rt.linear_stacked(x.cuda(), fmt, group, ntot, codes, scales, down=down.cuda(), up=up.cuda())
+    _compare(y, expected, (fmt, g, m))
+    resid = (torch.randn(m, ntot, generator=gen) * 0.5).half()
+    y2 = rt.linear_stacked(x.cuda(), fmt, group, ntot, codes, scales, down=down.cuda(), up=up.cuda(), residual=resid.cuda())
+    assert torch.equal(y2.cpu(), (y.float().cpu() + resid.float()).half())
+    with pytest.raises(ValueError):
+        rt.linear_stacked(torch.zeros(65, k, dtype=torch.float16, device='cuda'), fmt, group, ntot, codes, scales)

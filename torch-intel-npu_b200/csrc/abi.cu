@@ -17,11 +17,12 @@ cudaError_t launch_dequantize(int fmt, int group, int n, int k, const uint8_t *c
                               uint16_t *out, cudaStream_t stream);
 // gemv.cu
 bool gemv_supported(int fmt, int group, int m, int n, int k);
-cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, const uint16_t *v, uint16_t *z,
+cudaError_t launch_lowrank_project(int m, int k, int rank, int zs, const uint16_t *x, const uint16_t *v, uint16_t *z,
                                    cudaStream_t st);
 cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                        const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
-                        uint16_t *y, void *scratch, int *counters, cudaStream_t st);
+                        const uint16_t *scales, const uint16_t *z, int zs, const uint16_t *up, int rank,
+                        const uint16_t *bias, const uint16_t *resid, uint16_t *y, void *scratch, int *counters,
+                        cudaStream_t st);
 size_t gemv_workspace_bytes(int fmt, int m, int n, int k);
 cudaError_t launch_linear_generic(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
                                   const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank,
@@ -118,7 +119,8 @@ int select_path(int fmt, int group, int m, int n, int k, int rank) {
   return LB_PATH_GENERIC;
 }
 
-size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * 32 * 2) : 0; }
+// z holds rank rounded up to 32 columns per activation row (32 for every lb_linear call).
+size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * ((rank + 31) / 32 * 32) * 2) : 0; }
 
 // z projection for the TC path at larger M runs on the tensor cores too
 bool z_on_tc(int m, int k, int rank) { return m > 32 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0); }
@@ -271,13 +273,13 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
         e = launch_tc(LB_FMT_FP16, k, m, rank, k, x, reinterpret_cast<const uint8_t *>(down), nullptr, nullptr,
                       nullptr, 0, nullptr, z, 32, zpart, reinterpret_cast<int *>(ws + kCounterOffset), err, st);
     } else {
-      e = launch_lowrank_project(m, k, rank, x, down, z, st);
+      e = launch_lowrank_project(m, k, rank, 32, x, down, z, st);
     }
     if (e != cudaSuccess) return cuda_status(e);
   }
   switch (path) {
     case LB_PATH_GEMV:
-      e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, rest,
+      e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, 32, up, rank, bias, nullptr, y, rest,
                       reinterpret_cast<int *>(ws + kCounterOffset), st);
       break;
     case LB_PATH_TC:
@@ -294,6 +296,41 @@ int lb_linear(int fmt, int group, int m, int n, int k, const uint16_t *x, const 
               size_t workspace_bytes, void *stream) {
   return lb_linear_path(LB_PATH_AUTO, fmt, group, m, n, k, x, codes, scales, down, up, rank, bias, y, workspace,
                         workspace_bytes, stream);
+}
+
+int lb_linear_stacked(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                      const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank, const uint16_t *bias,
+                      const uint16_t *residual, uint16_t *y, void *workspace, size_t workspace_bytes, void *stream) {
+  if (injected("lb_linear_stacked")) return LB_ERR_INJECTED;
+  if (!valid_format(fmt) || m < 1 || n < 1 || k < 1 || !x || !codes || !y) return LB_ERR_INVALID_ARGUMENT;
+  if (fmt != LB_FMT_FP16 && (!scales || group < 1 || group > k || k % group)) return LB_ERR_INVALID_ARGUMENT;
+  if ((down == nullptr) != (up == nullptr)) return LB_ERR_INVALID_ARGUMENT;
+  if (down && (rank < 1 || rank > 128 || rank > k)) return LB_ERR_INVALID_ARGUMENT;
+  if (int64_t(m) * k > (int64_t(1) << 40) || int64_t(n) * k > (int64_t(1) << 40)) return LB_ERR_INVALID_ARGUMENT;
+  if (!down) rank = 0;
+  if (fmt == LB_FMT_FP16) group = k;
+  if (!gemv_supported(fmt, group, m, n, k) || !aligned16(x) || !aligned16(codes) || !aligned16(y) ||
+      !aligned16(workspace) || (down && (!aligned16(down) || !aligned16(up))))
+    return LB_ERR_UNSUPPORTED;
+  const size_t need = kHeader + z_bytes(m, rank) + align256(gemv_workspace_bytes(fmt, m, n, k));
+  if (!workspace || workspace_bytes < need) return LB_ERR_WORKSPACE;
+  const size_t yb = size_t(m) * n * 2;
+  if (overlaps(y, yb, x, size_t(m) * k * 2) || overlaps(y, yb, codes, code_bytes(fmt, n, k)) ||
+      (scales && overlaps(y, yb, scales, size_t(n) * (k / group) * 2)) ||
+      (bias && overlaps(y, yb, bias, size_t(n) * 2)) || (down && overlaps(y, yb, down, size_t(rank) * k * 2)) ||
+      (up && overlaps(y, yb, up, size_t(n) * rank * 2)) || (residual && overlaps(y, yb, residual, yb)) ||
+      overlaps(y, yb, workspace, need))
+    return LB_ERR_ALIAS;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const int zs = (rank + 31) / 32 * 32;
+  uint16_t *z = rank > 0 ? reinterpret_cast<uint16_t *>(ws + kHeader) : nullptr;
+  cudaError_t e = cudaSuccess;
+  if (z) e = launch_lowrank_project(m, k, rank, zs, x, down, z, st);
+  if (e == cudaSuccess)
+    e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, zs, up, rank, bias, residual, y,
+                    ws + kHeader + z_bytes(m, rank), reinterpret_cast<int *>(ws + kCounterOffset), st);
+  return cuda_status(e);
 }
 
 int lb_workspace_status(const void *workspace, void *stream) {

@@ -36,9 +36,11 @@ struct GemvParams {
   const __half *x;       // [m, k]
   const uint8_t *codes;  // packed rows, canonical reference layout
   const __half *scales;  // [n, k/group] (unused for FP16)
-  const __half *z;       // [m, 32] correction projection half(x . V^T), or null
+  const __half *z;       // [m, zs] correction projection half(x . V^T), zero past rank, or null
   const __half *up;      // [n, rank]
-  int rank;
+  int rank;              // <= zs
+  int zs;                // z row stride: rank rounded up to a multiple of 32 (<= 128)
+  const __half *resid;   // [m, n] added last (half(y + resid)), or null
   const __half *bias;    // [n] or null
   __half *y;             // [m, n]
   int warps_k;           // warps splitting a CTA's K range (1, 2, 4, 8)
@@ -286,47 +288,46 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       if (per_row_scale) v *= __half2float(p.scales[n]);
       __half yq = __float2half_rn(v);
       if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
+      if (p.resid) yq = __float2half_rn(__half2float(yq) + __half2float(p.resid[int64_t(mm) * p.n + n]));
       p.y[int64_t(mm) * p.n + n] = yq;
     }
     return;
   }
 
   // Correction delta = half(z . U[n]^T) on the tensor cores: per 16-row group, U rows
-  // (rank padded to 32 with zeros) are the A operand and z (zero beyond the rank) the
-  // B operand, two m16n8k16 tiles per 8-column group; then
-  // y = half(half(half(acc) + bias) + delta) as torch_npu_smollm.py:150-164 stages it.
+  // (rank padded to zs with zeros) are the A operand and z (zero beyond the rank) the B
+  // operand, zs / 16 m16n8k16 tiles per 8-column group; then
+  // y = half(half(half(acc) + bias) + delta) as torch_npu_smollm.py:150-164 stages it, and
+  // half(y + residual) when a residual is fused (torch_npu_smollm.py:192).
+  const int ktiles = p.zs / 16;
   for (int rg = warp; rg < rows_cta / 16; rg += kWarps) {
     const int rl0 = rg * 16;
-    uint32_t ua[2][4];
-#pragma unroll
-    for (int kt = 0; kt < 2; ++kt) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = row0 + rl0 + g + 8 * (i & 1);
-        const int kk = 16 * kt + 2 * t + 8 * (i >> 1);
-        __half lo = __float2half(0.f), hi = lo;
-        if (row < p.n) {
-          const __half *ur = p.up + int64_t(row) * p.rank;
-          if (kk < p.rank) lo = ur[kk];
-          if (kk + 1 < p.rank) hi = ur[kk + 1];
-        }
-        ua[kt][i] = h2_as_u32(__halves2half2(lo, hi));
-      }
-    }
 #pragma unroll
     for (int c = 0; c < NCOL; ++c) {
       if (8 * c >= p.m) break;
       const int mz = 8 * c + g;   // activation row of this lane's B column
       float d[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int kt = 0; kt < ktiles; ++kt) {
+        uint32_t ua[4];
 #pragma unroll
-      for (int kt = 0; kt < 2; ++kt) {
+        for (int i = 0; i < 4; ++i) {
+          const int row = row0 + rl0 + g + 8 * (i & 1);
+          const int kk = 16 * kt + 2 * t + 8 * (i >> 1);
+          __half lo = __float2half(0.f), hi = lo;
+          if (row < p.n) {
+            const __half *ur = p.up + int64_t(row) * p.rank;
+            if (kk < p.rank) lo = ur[kk];
+            if (kk + 1 < p.rank) hi = ur[kk + 1];
+          }
+          ua[i] = h2_as_u32(__halves2half2(lo, hi));
+        }
         uint32_t b0 = 0, b1 = 0;
         if (mz < p.m) {
-          const uint32_t *zr = reinterpret_cast<const uint32_t *>(p.z + mz * 32);
+          const uint32_t *zr = reinterpret_cast<const uint32_t *>(p.z + int64_t(mz) * p.zs);
           b0 = zr[8 * kt + t];
           b1 = zr[8 * kt + t + 4];
         }
-        mma16816(d, ua[kt], b0, b1);
+        mma16816(d, ua, b0, b1);
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -337,15 +338,17 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         __half yq = __float2half_rn(v);
         if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
         yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(d[i])));
+        if (p.resid) yq = __float2half_rn(__half2float(yq) + __half2float(p.resid[int64_t(mm) * p.n + n]));
         p.y[int64_t(mm) * p.n + n] = yq;
       }
     }
   }
 }
 
-// z[m, r] = half(sum_k x[m,k] V[r,k]) for r < rank (zero for rank <= r < 32):
+
+// z[m, r] = half(sum_k x[m,k] V[r,k]) for r < rank (zero for rank <= r < zs), row stride zs:
 // one CTA per (r, m-tile of up to 8 rows); 8 warps split K, 16-byte loads of V and x.
-__global__ void __launch_bounds__(256) lowrank_project_kernel(int m, int k, int rank, const __half *__restrict__ x,
+__global__ void __launch_bounds__(256) lowrank_project_kernel(int m, int k, int rank, int zs, const __half *__restrict__ x,
                                                               const __half *__restrict__ v, __half *__restrict__ z) {
   __shared__ float red[8][8];
   const int r = blockIdx.x, m0 = blockIdx.y * 8;
@@ -380,7 +383,7 @@ __global__ void __launch_bounds__(256) lowrank_project_kernel(int m, int k, int 
   if (threadIdx.x < 8 && m0 + threadIdx.x < m) {
     float s = 0.f;
     for (int w = 0; w < 8; ++w) s += red[w][threadIdx.x];
-    z[int64_t(m0 + threadIdx.x) * 32 + r] = __float2half_rn(r < rank ? s : 0.f);
+    z[int64_t(m0 + threadIdx.x) * zs + r] = __float2half_rn(r < rank ? s : 0.f);
   }
 }
 
@@ -427,20 +430,20 @@ __global__ void linear_generic_kernel(int fmt, int m, int n, int k, int group, c
 }
 
 // generic z projection for any K
-__global__ void lowrank_project_generic_kernel(int m, int k, int rank, const __half *__restrict__ x,
+__global__ void lowrank_project_generic_kernel(int m, int k, int rank, int zs, const __half *__restrict__ x,
                                                const __half *__restrict__ v, __half *__restrict__ z) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   pdl_launch();
   pdl_wait();
-  if (warp >= int64_t(m) * 32) return;
-  const int mm = int(warp / 32), r = int(warp % 32);
+  if (warp >= int64_t(m) * zs) return;
+  const int mm = int(warp / zs), r = int(warp % zs);
   float acc = 0.f;
   if (r < rank)
     for (int kk = lane; kk < k; kk += 32)
       acc = fmaf(__half2float(x[int64_t(mm) * k + kk]), __half2float(v[int64_t(r) * k + kk]), acc);
   acc = warp_sum(acc);
-  if (lane == 0) z[mm * 32 + r] = __float2half_rn(acc);
+  if (lane == 0) z[int64_t(mm) * zs + r] = __float2half_rn(acc);
 }
 
 }  // namespace lowbit
@@ -536,16 +539,17 @@ static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_
   }
 }
 
-cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, const uint16_t *v, uint16_t *z,
+// zs: z row stride (rank rounded up to 32; the columns past the rank are written as zero).
+cudaError_t launch_lowrank_project(int m, int k, int rank, int zs, const uint16_t *x, const uint16_t *v, uint16_t *z,
                                    cudaStream_t st) {
   const bool vec = k % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(v) & 15u) == 0;
   if (vec)
-    return launch_k(lowrank_project_kernel, dim3(32, (m + 7) / 8), dim3(256), 0, st, m, k, rank,
+    return launch_k(lowrank_project_kernel, dim3(zs, (m + 7) / 8), dim3(256), 0, st, m, k, rank, zs,
                     reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
                     reinterpret_cast<__half *>(z));
-  const int64_t warps = int64_t(m) * 32;
+  const int64_t warps = int64_t(m) * zs;
   return launch_k(lowrank_project_generic_kernel, dim3(unsigned((warps * 32 + 255) / 256)), dim3(256), 0, st, m, k,
-                  rank, reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
+                  rank, zs, reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
                   reinterpret_cast<__half *>(z));
 }
 
@@ -553,8 +557,9 @@ cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, co
 // array of kMaxGemvCounters at a fixed place in the workspace, zero before the first call
 // and left at zero by every call.
 cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                        const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
-                        uint16_t *y, void *scratch, int *counters, cudaStream_t st) {
+                        const uint16_t *scales, const uint16_t *z, int zs, const uint16_t *up, int rank,
+                        const uint16_t *bias, const uint16_t *resid, uint16_t *y, void *scratch, int *counters,
+                        cudaStream_t st) {
   GemvParams p = {};
   p.m = m; p.n = n; p.k = k; p.group = fmt == LB_FMT_FP16 ? k : group;
   p.x = reinterpret_cast<const __half *>(x);
@@ -563,7 +568,9 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   p.z = reinterpret_cast<const __half *>(z);
   p.up = reinterpret_cast<const __half *>(up);
   p.rank = rank;
+  p.zs = zs;
   p.bias = reinterpret_cast<const __half *>(bias);
+  p.resid = reinterpret_cast<const __half *>(resid);
   p.y = reinterpret_cast<__half *>(y);
   const GemvPlan pl = gemv_plan(fmt, m, n, k);
   p.warps_k = pl.warps_k;

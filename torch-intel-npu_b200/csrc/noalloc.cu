@@ -19,11 +19,12 @@
 namespace lowbit_host {
 bool gemv_supported(int fmt, int group, int m, int n, int k);
 size_t gemv_workspace_bytes(int fmt, int m, int n, int k);
-cudaError_t launch_lowrank_project(int m, int k, int rank, const uint16_t *x, const uint16_t *v, uint16_t *z,
+cudaError_t launch_lowrank_project(int m, int k, int rank, int zs, const uint16_t *x, const uint16_t *v, uint16_t *z,
                                    cudaStream_t st);
 cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                        const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank, const uint16_t *bias,
-                        uint16_t *y, void *scratch, int *counters, cudaStream_t st);
+                        const uint16_t *scales, const uint16_t *z, int zs, const uint16_t *up, int rank,
+                        const uint16_t *bias, const uint16_t *resid, uint16_t *y, void *scratch, int *counters,
+                        cudaStream_t st);
 }  // namespace lowbit_host
 
 namespace {
@@ -89,9 +90,10 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
   uint16_t *z = nullptr;
   if (e == cudaSuccess && rank > 0) {
     z = reinterpret_cast<uint16_t *>(s + kZOffset);
-    e = launch_lowrank_project(m, k, rank, x, down, z, st);
+    e = launch_lowrank_project(m, k, rank, 32, x, down, z, st);
   }
   if (e == cudaSuccess)
-    e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, up, rank, bias, y, s + kPartialOffset, counters, st);
+    e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, 32, up, rank, bias, nullptr, y, s + kPartialOffset,
+                    counters, st);
   return e == cudaSuccess ? LB_OK : LB_ERR_CUDA;
 }

@@ -38,6 +38,7 @@ SIGNATURES = {
     'lb_linear': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_path': ([_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_select': ([_I, _I, _I, _I, _I, _I], _I),
+    'lb_linear_stacked': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _S, _P], _I),
     'lb_rmsnorm': ([_P, _P, _P, _P, _P, _I, _I, _F, _P], _I),
     'lb_rope': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     'lb_kv_append': ([_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _P], _I),
@@ -198,6 +199,24 @@ def linear(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, ou
     status = L.lb_linear_path(PATH[path], LB_FMT[fmt], group, m, n, k, ptr(x), ptr(codes), ptr(scales), ptr(down),
                               ptr(up), rank, ptr(bias), ptr(y), ptr(ws), ws.numel(), stream_ptr(x.device))
     check(status, 'lb_linear')
+    return y
+
+
+def linear_stacked(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, residual=None, out=None):
+    """One decode-GEMV launch over several stacked linears (lb_linear_stacked): codes /
+    scales / bias are the row-wise concatenation, down / up the block-diagonal stack of
+    their corrections (rank <= 128); residual [M, N] is added last."""
+    L = require_cuda()
+    x = _contig_cuda(x, 'x', torch.float16)
+    m, k = x.shape
+    rank = 0 if down is None else down.shape[0]
+    y = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=x.device)
+    if residual is not None:
+        residual = _contig_cuda(residual, 'residual', torch.float16)
+    ws = Workspace.get(L.lb_linear_workspace_bytes(LB_FMT[fmt], group, m, n, k, rank), x.device)
+    status = L.lb_linear_stacked(LB_FMT[fmt], group, m, n, k, ptr(x), ptr(codes), ptr(scales), ptr(down), ptr(up),
+                                 rank, ptr(bias), ptr(residual), ptr(y), ptr(ws), ws.numel(), stream_ptr(x.device))
+    check(status, 'lb_linear_stacked')
     return y
 
 

@@ -31,6 +31,8 @@ import lowbit_runtime as rt
 from torch_npu_lowbit import PackedWeight, quantize_weight_device
 from torch_npu_lowbit_correction import LowRankCorrection
 
+_STACKS = {'qkv': ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight'),
+           'gate_up': ('mlp.gate_proj.weight', 'mlp.up_proj.weight')}
 _PROJECTIONS = ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight',
                 'self_attn.o_proj.weight', 'mlp.gate_proj.weight', 'mlp.up_proj.weight', 'mlp.down_proj.weight')
 _NORMS = ('input_layernorm.weight', 'post_attention_layernorm.weight')
@@ -176,6 +178,7 @@ class FrozenSmolLayer(torch.nn.Module):
                 entry['down'], entry['up'] = down.to(self.device), up.to(self.device)
             self._proj[name] = entry
         self._norm = {name: weights[name].detach().to(self.device, torch.float16).contiguous() for name in _NORMS}
+        self._stacks = {key: self._stack(names) for key, names in _STACKS.items()}
         self._tp = tp_group
         self._row_corr = {}
         for name, (down, up) in (row_corrections or {}).items():
@@ -187,6 +190,49 @@ class FrozenSmolLayer(torch.nn.Module):
 
     mode = property(lambda self: self._mode)
     fp16_projections = property(lambda self: self._fp16_projections)
+
+    def _stack(self, names):
+        """q/k/v (or gate/up) as one decode-GEMV launch (lb_linear_stacked): rows stacked in
+        one code buffer (the single-projection entries become views of it), corrections as
+        one block-diagonal correction of rank 32 per projection.  None when the projections
+        differ in format or group (e.g. an fp16 exception)."""
+        ents = [self._proj[n] for n in names]
+        if len({(e['fmt'], e['group'], e['k']) for e in ents}) != 1:
+            return None
+        k = ents[0]['k']
+        codes = torch.cat([e['codes'] for e in ents])
+        scales = None if ents[0]['scales'] is None else torch.cat([e['scales'] for e in ents])
+        off_c = off_s = 0
+        for e in ents:   # share the stacked storage (offsets are 16-byte multiples here)
+            nc, ns = e['codes'].numel(), 0 if scales is None else e['scales'].numel()
+            if off_c % 16 == 0 and (off_s * 2) % 16 == 0:
+                e['codes'] = codes[off_c:off_c + nc]
+                if scales is not None:
+                    e['scales'] = scales[off_s:off_s + ns]
+            off_c, off_s = off_c + nc, off_s + ns
+        n = sum(e['n'] for e in ents)
+        down = up = None
+        if any(e['down'] is not None for e in ents):
+            rank = 32 * len(ents)
+            down = torch.zeros(rank, k, dtype=torch.float16, device=self.device)
+            up = torch.zeros(n, rank, dtype=torch.float16, device=self.device)
+            row = 0
+            for i, e in enumerate(ents):
+                if e['down'] is not None:
+                    r = e['down'].shape[0]
+                    down[32 * i:32 * i + r] = e['down']
+                    up[row:row + e['n'], 32 * i:32 * i + r] = e['up']
+                row += e['n']
+        return dict(fmt=ents[0]['fmt'], group=ents[0]['group'], n=n, k=k, codes=codes, scales=scales, down=down,
+                    up=up, widths=[e['n'] for e in ents])
+
+    def _stacked(self, key, x, residual=None):
+        """The stacked launch when it applies (decode batch <= 64), else None."""
+        st = self._stacks.get(key)
+        if st is None or rt.linear_select(st['fmt'], st['group'], x.shape[0], st['n'], st['k']) != 'gemv':
+            return None
+        return rt.linear_stacked(x, st['fmt'], st['group'], st['n'], st['codes'], st['scales'], down=st['down'],
+                                 up=st['up'], residual=residual)
 
     # ---- building blocks -------------------------------------------------------------
     def linear(self, name, x, out=None):
@@ -239,23 +285,45 @@ class FrozenSmolLayer(torch.nn.Module):
         return out.transpose(1, 2).reshape(b * s, cfg.heads * cfg.head_dim)
 
     def _qkv(self, normed, positions, rope):
-        q = self.linear('self_attn.q_proj.weight', normed)
-        k = self.linear('self_attn.k_proj.weight', normed)
-        v = self.linear('self_attn.v_proj.weight', normed)
+        """q, k, v after RoPE (row views of one buffer when the stacked launch ran)."""
+        qkv = self._stacked('qkv', normed)
+        if qkv is not None:
+            nq, nk, _ = self._stacks['qkv']['widths']
+            q, k, v = qkv[:, :nq], qkv[:, nq:nq + nk], qkv[:, nq + nk:]
+        else:
+            q = self.linear('self_attn.q_proj.weight', normed)
+            k = self.linear('self_attn.k_proj.weight', normed)
+            v = self.linear('self_attn.v_proj.weight', normed)
         cfg = self.config
         cos, sin = rope
         rt.check(rt.lib().lb_rope(rt.ptr(q), rt.ptr(k), rt.ptr(positions), rt.ptr(cos), rt.ptr(sin), cos.shape[0], q.shape[0],
-                                  cfg.heads, cfg.kv_heads, cfg.head_dim, q.shape[1], k.shape[1], rt.stream_ptr(q.device)),
+                                  cfg.heads, cfg.kv_heads, cfg.head_dim, q.stride(0), k.stride(0), rt.stream_ptr(q.device)),
                  'lb_rope')
         return q, k, v
 
-    def _ffn(self, normed):
-        gate = self.linear('mlp.gate_proj.weight', normed)
-        up = self.linear('mlp.up_proj.weight', normed)
-        act = torch.empty_like(gate)
-        rt.check(rt.lib().lb_silu_mul(rt.ptr(gate), rt.ptr(up), gate.shape[1], rt.ptr(act), gate.shape[0], gate.shape[1],
+    def _ffn(self, normed, residual=None):
+        """down(silu(gate) * up); with ``residual`` the stacked path returns
+        half(residual + down) from the down projection's epilogue, else None is returned
+        as the second value and the caller adds."""
+        gu = self._stacked('gate_up', normed)
+        if gu is not None:
+            ni = self._stacks['gate_up']['widths'][0]
+            gate, up = gu[:, :ni], gu[:, ni:]
+        else:
+            gate = self.linear('mlp.gate_proj.weight', normed)
+            up = self.linear('mlp.up_proj.weight', normed)
+        rows, cols = gate.shape
+        act = torch.empty(rows, cols, dtype=torch.float16, device=gate.device)
+        rt.check(rt.lib().lb_silu_mul(rt.ptr(gate), rt.ptr(up), gate.stride(0), rt.ptr(act), rows, cols,
                                       rt.stream_ptr(gate.device)), 'lb_silu_mul')
-        return self.linear('mlp.down_proj.weight', act)
+        name = 'mlp.down_proj.weight'
+        p = self._proj[name]
+        if residual is not None and self._tp is None and \
+                rt.linear_select(p['fmt'], p['group'], rows, p['n'], p['k']) == 'gemv':
+            out = rt.linear_stacked(act, p['fmt'], p['group'], p['n'], p['codes'], p['scales'], down=p['down'],
+                                    up=p['up'], residual=residual)
+            return out, True
+        return self.linear(name, act), False
 
     def _check_input(self, x):
         if self.training:
@@ -281,7 +349,7 @@ class FrozenSmolLayer(torch.nn.Module):
         o = self.linear('self_attn.o_proj.weight', attn)
         h1 = torch.empty_like(h)
         normed = self.norm(o, 'post_attention_layernorm.weight', residual=h, residual_out=h1)
-        down = self._ffn(normed)
+        down, _ = self._ffn(normed)
         out = torch.empty_like(h)
         rt.check(rt.lib().lb_add(rt.ptr(h1), rt.ptr(down), rt.ptr(out), out.numel(), rt.stream_ptr(out.device)), 'lb_add')
         return out.view(b, s, d), k, v
@@ -338,16 +406,18 @@ class FrozenSmolLayer(torch.nn.Module):
         q, k, v = self._qkv(normed, lengths, self._rope())
         L = rt.lib()
         st = rt.stream_ptr(h.device)
-        rt.check(L.lb_kv_append(rt.ptr(k), rt.ptr(v), k.shape[1], rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), b,
+        rt.check(L.lb_kv_append(rt.ptr(k), rt.ptr(v), k.stride(0), rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), b,
                                 cfg.kv_heads, cfg.head_dim, self.max_positions, st), 'lb_kv_append')
         attn = torch.empty(b, cfg.heads * cfg.head_dim, dtype=torch.float16, device=h.device)
-        rt.check(L.lb_attention_decode(rt.ptr(q), q.shape[1], rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), rt.ptr(attn),
+        rt.check(L.lb_attention_decode(rt.ptr(q), q.stride(0), rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), rt.ptr(attn),
                                        b, cfg.heads, cfg.kv_heads, cfg.head_dim, self.max_positions,
                                        1.0 / cfg.head_dim ** 0.5, None, 0, st), 'lb_attention_decode')
         o = self.linear('self_attn.o_proj.weight', attn)
         h1 = torch.empty_like(h)
         normed = self.norm(o, 'post_attention_layernorm.weight', residual=h, residual_out=h1)
-        down = self._ffn(normed)
+        down, fused = self._ffn(normed, residual=h1)
+        if fused:
+            return down
         out = torch.empty_like(h)
         rt.check(L.lb_add(rt.ptr(h1), rt.ptr(down), rt.ptr(out), out.numel(), st), 'lb_add')
         return out
