@@ -174,6 +174,18 @@ int lb_attention_decode(const uint16_t *q, int q_stride, const uint16_t *k_cache
                         int heads, int kv_heads, int head_dim, int max_pos, float scale,
                         void *workspace, size_t workspace_bytes, void *stream);
 size_t lb_attention_workspace_bytes(int batch, int heads, int max_pos);
+/* lb_rope of this step's q and k + lb_kv_append + lb_attention_decode as one launch
+ * (torch_npu_smollm.py:174-182, :288-292).  No single reference call: the attention CTA
+ * of (b, kv head) rotates and appends that head's new k row (and copies v) at position
+ * lengths[b], then rotates q while loading it; same fp16 staging as the three calls.
+ * k_new / v_new: [B, kv_stride] rows (column blocks of one q|k|v buffer allowed); q is
+ * read, not written.  Positions at or past table_rows are attended unrotated. */
+int lb_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new,
+                             const uint16_t *v_new, int kv_stride, const uint16_t *cos_table,
+                             const uint16_t *sin_table, int table_rows, uint16_t *k_cache,
+                             uint16_t *v_cache, const int32_t *lengths, uint16_t *out, int batch,
+                             int heads, int kv_heads, int head_dim, int max_pos, float scale,
+                             void *stream);
 /* h = half(half(silu(float(gate))) * up)  (torch_npu_smollm.py:189-190); gate/up may be
  * column blocks of one [rows, 2F] buffer (row stride in elements). */
 int lb_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows,

@@ -180,3 +180,44 @@ def test_session_graph_is_reused_across_generate_calls():
     b = model.generate(ids, 10)
     assert model.session(2)['graph'] is graph
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize('heads,kv,b', [(9, 3, 2), (15, 5, 64), (32, 32, 3)])
+def test_fused_rope_append_attention_equals_separate_calls(heads, kv, b):
+    """lb_attention_decode_rope == lb_rope + lb_kv_append + lb_attention_decode, bitwise,
+    for q/k/v as column blocks of one buffer; a position past the RoPE table stays
+    unrotated in both."""
+    import lowbit_runtime as rt
+    import torch_npu_smollm as sm
+    L, st = rt.lib(), rt.stream_ptr()
+    hd, max_pos = 64, 96
+    cfg = sm.SmolConfig.from_dict(small_config(hidden=heads * hd, heads=heads, kv=kv))
+    cos, sin = sm.rope_tables(cfg, 80, 'cuda')            # table shorter than the cache
+    gen = torch.Generator().manual_seed(heads + b)
+    nq, nk = heads * hd, kv * hd
+    qkv = (torch.randn(b, nq + 2 * nk, generator=gen) * 0.5).half().cuda()
+    lengths = torch.randint(0, 90, (b,), generator=gen, dtype=torch.int32).cuda()
+    lengths[0] = 85                                       # past the table: unrotated
+    caches = (torch.randn(2, b, kv, max_pos, hd, generator=gen) * 0.5).half().cuda()
+    scale = 1.0 / hd ** 0.5
+    # separate calls on copies
+    sep = qkv.clone()
+    kc1, vc1 = caches[0].clone(), caches[1].clone()
+    q1, k1, v1 = sep[:, :nq], sep[:, nq:nq + nk], sep[:, nq + nk:]
+    rt.check(L.lb_rope(rt.ptr(q1), rt.ptr(k1), rt.ptr(lengths), rt.ptr(cos), rt.ptr(sin), cos.shape[0], b, heads, kv, hd,
+                       sep.stride(0), sep.stride(0), st), 'lb_rope')
+    rt.check(L.lb_kv_append(rt.ptr(k1), rt.ptr(v1), sep.stride(0), rt.ptr(kc1), rt.ptr(vc1), rt.ptr(lengths), b, kv, hd,
+                            max_pos, st), 'lb_kv_append')
+    out1 = torch.empty(b, nq, dtype=torch.float16, device='cuda')
+    rt.check(L.lb_attention_decode(rt.ptr(q1), sep.stride(0), rt.ptr(kc1), rt.ptr(vc1), rt.ptr(lengths), rt.ptr(out1), b,
+                                   heads, kv, hd, max_pos, scale, None, 0, st), 'lb_attention_decode')
+    # fused
+    kc2, vc2 = caches[0].clone(), caches[1].clone()
+    q2, k2, v2 = qkv[:, :nq], qkv[:, nq:nq + nk], qkv[:, nq + nk:]
+    out2 = torch.empty(b, nq, dtype=torch.float16, device='cuda')
+    rt.check(L.lb_attention_decode_rope(rt.ptr(q2), qkv.stride(0), rt.ptr(k2), rt.ptr(v2), qkv.stride(0), rt.ptr(cos),
+                                        rt.ptr(sin), cos.shape[0], rt.ptr(kc2), rt.ptr(vc2), rt.ptr(lengths), rt.ptr(out2),
+                                        b, heads, kv, hd, max_pos, scale, st), 'lb_attention_decode_rope')
+    torch.cuda.synchronize()
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    assert torch.equal(out1, out2)

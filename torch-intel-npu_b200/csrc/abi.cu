@@ -42,6 +42,10 @@ cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint
 cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *kc, uint16_t *vc,
                              const int32_t *lengths, int batch, int kvh, int hd, int max_pos, cudaStream_t st);
 size_t attention_smem(int heads, int kvh, int max_pos);
+cudaError_t launch_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
+                                         int kv_stride, const uint16_t *cos_t, const uint16_t *sin_t, int table_rows,
+                                         uint16_t *kc, uint16_t *vc, const int32_t *lengths, uint16_t *out, int batch,
+                                         int heads, int kvh, int hd, int max_pos, float scale, cudaStream_t st);
 cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
                                     const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
                                     int max_pos, float scale, cudaStream_t st);
@@ -389,6 +393,28 @@ int lb_attention_decode(const uint16_t *q, int q_stride, const uint16_t *k_cache
   if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q) || q_stride % 8) return LB_ERR_INVALID_ARGUMENT;
   return cuda_status(launch_attention_decode(q, q_stride, k_cache, v_cache, lengths, out, batch, heads, kv_heads,
                                              head_dim, max_pos, scale, static_cast<cudaStream_t>(stream)));
+}
+
+int lb_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
+                             int kv_stride, const uint16_t *cos_table, const uint16_t *sin_table, int table_rows,
+                             uint16_t *k_cache, uint16_t *v_cache, const int32_t *lengths, uint16_t *out, int batch,
+                             int heads, int kv_heads, int head_dim, int max_pos, float scale, void *stream) {
+  if (injected("lb_attention_decode_rope")) return LB_ERR_INJECTED;
+  if (!q || !k_new || !v_new || !cos_table || !sin_table || !k_cache || !v_cache || !lengths || !out || batch < 1 ||
+      heads < 1 || kv_heads < 1 || heads % kv_heads || heads / kv_heads > 8 || head_dim != 64 || max_pos < 1 ||
+      table_rows < 1 || q_stride < heads * head_dim || kv_stride < kv_heads * head_dim ||
+      attention_smem(heads, kv_heads, max_pos) > 160 * 1024)
+    return LB_ERR_INVALID_ARGUMENT;
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q) || q_stride % 8) return LB_ERR_INVALID_ARGUMENT;
+  // strided row blocks: the last row ends width elements after its start
+  const size_t ob = size_t(batch) * heads * head_dim * 2;
+  const size_t qb = (size_t(batch - 1) * q_stride + size_t(heads) * head_dim) * 2;
+  const size_t kb = (size_t(batch - 1) * kv_stride + size_t(kv_heads) * head_dim) * 2;
+  if (overlaps(out, ob, q, qb) || overlaps(out, ob, k_new, kb) || overlaps(out, ob, v_new, kb))
+    return LB_ERR_ALIAS;
+  return cuda_status(launch_attention_decode_rope(q, q_stride, k_new, v_new, kv_stride, cos_table, sin_table,
+                                                  table_rows, k_cache, v_cache, lengths, out, batch, heads, kv_heads,
+                                                  head_dim, max_pos, scale, static_cast<cudaStream_t>(stream)));
 }
 
 int lb_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,

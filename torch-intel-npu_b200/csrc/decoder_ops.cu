@@ -128,18 +128,28 @@ __global__ void kv_append_kernel(const __half *__restrict__ k, const __half *__r
   }
 }
 
+// Optional prologue of the decode attention: RoPE of this step's q and k and the KV append
+// (torch_npu_smollm.py:174-177, :288-292) done by the attention CTA that owns the kv head.
+struct RopeAppend {
+  const __half *k_new, *v_new;   // [B, kv_stride] rows of the new token; null: no prologue
+  int kv_stride;
+  const __half *cos_t, *sin_t;   // [table_rows, hd]
+  int table_rows;
+};
+
 // One-token GQA attention with the reference staging (torch_npu_smollm.py:178-182):
 // s_j = half(half(q.k_j) * scale); p = half(softmax_f32(s)); out = half(sum_j p_j v_j).
 // One CTA per (batch, kv head) serving the REP query heads that share it.  Keys and values
 // are read as 16-byte pieces (8 lanes per 128-byte row, 4 rows per warp) with kUnroll rows
 // per lane in flight, so a CTA keeps ~128 rows of loads outstanding per phase.
 template <int HD, int REP>
+// kc / vc are written by the prologue and read back in the same kernel, so they are not
+// declared read-only (no non-coherent loads of the appended row).
 __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__restrict__ q, int q_stride,
-                                                               const __half *__restrict__ kc,
-                                                               const __half *__restrict__ vc,
+                                                               __half *kc, __half *vc,
                                                                const int32_t *__restrict__ lengths,
                                                                __half *__restrict__ out, int heads, int kvh,
-                                                               int max_pos, float scale) {
+                                                               int max_pos, float scale, const RopeAppend ra) {
   static_assert(HD == 64, "rows are 8 lanes x 8 halves");
   constexpr int kUnroll = 4;
   extern __shared__ float sc[];  // [REP][max_pos]
@@ -148,15 +158,58 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__r
   pdl_launch();
   pdl_wait();
   const int b = blockIdx.x / kvh, g = blockIdx.x % kvh;
-  const int len = min(lengths[b] + 1, max_pos);
+  const int pos = lengths[b];
+  const int len = min(pos + 1, max_pos);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int sub = lane >> 3, l8 = lane & 7;
-  const __half *kbase = kc + (int64_t(b) * kvh + g) * max_pos * HD;
-  const __half *vbase = vc + (int64_t(b) * kvh + g) * max_pos * HD;
+  __half *kbase = kc + (int64_t(b) * kvh + g) * max_pos * HD;
+  __half *vbase = vc + (int64_t(b) * kvh + g) * max_pos * HD;
+  // RoPE staging v' = half(half(v cos) + half(rot(v) sin)), rot(v) = cat(-v[hd/2:], v[:hd/2]);
+  // positions outside the table are left unrotated, as lb_rope does
+  const bool rotate = ra.k_new != nullptr && pos >= 0 && pos < ra.table_rows;
+  if (ra.k_new != nullptr) {
+    if (threadIdx.x < HD / 2 && pos >= 0 && pos < max_pos) {
+      const int i = threadIdx.x;
+      const __half *kn = ra.k_new + int64_t(b) * ra.kv_stride + g * HD;
+      const __half *vn = ra.v_new + int64_t(b) * ra.kv_stride + g * HD;
+      __half *krow = kbase + int64_t(pos) * HD;
+      __half *vrow = vbase + int64_t(pos) * HD;
+      __half a = kn[i], c = kn[i + HD / 2];
+      if (rotate) {
+        const __half *ct = ra.cos_t + int64_t(pos) * HD, *st = ra.sin_t + int64_t(pos) * HD;
+        const __half a2 = __hadd(__hmul(a, ct[i]), __hmul(__hneg(c), st[i]));
+        c = __hadd(__hmul(c, ct[i + HD / 2]), __hmul(a, st[i + HD / 2]));
+        a = a2;
+      }
+      krow[i] = a;
+      krow[i + HD / 2] = c;
+      vrow[i] = vn[i];
+      vrow[i + HD / 2] = vn[i + HD / 2];
+    }
+    __syncthreads();   // the appended row is read back below by other threads of this CTA
+  }
   float qv[REP][8];
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
-    const uint4 qq = *reinterpret_cast<const uint4 *>(q + int64_t(b) * q_stride + (g * REP + r) * HD + l8 * 8);
+    uint4 qq = *reinterpret_cast<const uint4 *>(q + int64_t(b) * q_stride + (g * REP + r) * HD + l8 * 8);
+    if (rotate) {
+      // the partner half (element j +- hd/2) lives in lane l8 ^ 4 of the same 8-lane group
+      uint4 pp;
+      pp.x = __shfl_xor_sync(0xffffffffu, qq.x, 4);
+      pp.y = __shfl_xor_sync(0xffffffffu, qq.y, 4);
+      pp.z = __shfl_xor_sync(0xffffffffu, qq.z, 4);
+      pp.w = __shfl_xor_sync(0xffffffffu, qq.w, 4);
+      const __half *qh0 = reinterpret_cast<const __half *>(&qq), *ph = reinterpret_cast<const __half *>(&pp);
+      const __half *ct = ra.cos_t + int64_t(pos) * HD + l8 * 8, *st = ra.sin_t + int64_t(pos) * HD + l8 * 8;
+      uint4 rq;
+      __half *rh = reinterpret_cast<__half *>(&rq);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const __half part = l8 < 4 ? __hneg(ph[e]) : ph[e];
+        rh[e] = __hadd(__hmul(qh0[e], ct[e]), __hmul(part, st[e]));
+      }
+      qq = rq;
+    }
     const __half *qh = reinterpret_cast<const __half *>(&qq);
 #pragma unroll
     for (int e = 0; e < 8; ++e) qv[r][e] = __half2float(qh[e]);
@@ -360,33 +413,55 @@ cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride
 size_t attention_smem(int heads, int kvh, int max_pos) { return size_t(heads / kvh) * max_pos * sizeof(float); }
 
 template <int REP>
-static cudaError_t launch_attention_rep(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
+static cudaError_t launch_attention_rep(const uint16_t *q, int q_stride, uint16_t *kc, uint16_t *vc,
                                         const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh,
-                                        int max_pos, float scale, size_t smem, cudaStream_t st) {
+                                        int max_pos, float scale, size_t smem, const RopeAppend &ra, cudaStream_t st) {
   auto kern = attention_decode_kernel<64, REP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   return launch_k(kern, dim3(batch * kvh), dim3(256), smem, st, reinterpret_cast<const __half *>(q), q_stride,
-                  reinterpret_cast<const __half *>(kc), reinterpret_cast<const __half *>(vc), lengths,
-                  reinterpret_cast<__half *>(out), heads, kvh, max_pos, scale);
+                  reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), lengths,
+                  reinterpret_cast<__half *>(out), heads, kvh, max_pos, scale, ra);
+}
+
+static cudaError_t launch_attention(const uint16_t *q, int q_stride, uint16_t *kc, uint16_t *vc,
+                                    const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
+                                    int max_pos, float scale, const RopeAppend &ra, cudaStream_t st) {
+  if (hd != 64) return cudaErrorInvalidValue;
+  const size_t smem = attention_smem(heads, kvh, max_pos);
+  switch (heads / kvh) {
+    case 1: return launch_attention_rep<1>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 2: return launch_attention_rep<2>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 3: return launch_attention_rep<3>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 4: return launch_attention_rep<4>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 5: return launch_attention_rep<5>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 6: return launch_attention_rep<6>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 7: return launch_attention_rep<7>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    case 8: return launch_attention_rep<8>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
                                     const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
                                     int max_pos, float scale, cudaStream_t st) {
-  if (hd != 64) return cudaErrorInvalidValue;
-  const size_t smem = attention_smem(heads, kvh, max_pos);
-  switch (heads / kvh) {
-    case 1: return launch_attention_rep<1>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 2: return launch_attention_rep<2>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 3: return launch_attention_rep<3>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 4: return launch_attention_rep<4>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 5: return launch_attention_rep<5>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 6: return launch_attention_rep<6>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 7: return launch_attention_rep<7>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    case 8: return launch_attention_rep<8>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, st);
-    default: return cudaErrorInvalidValue;
-  }
+  // without the prologue nothing writes the caches
+  return launch_attention(q, q_stride, const_cast<uint16_t *>(kc), const_cast<uint16_t *>(vc), lengths, out, batch,
+                          heads, kvh, hd, max_pos, scale, RopeAppend{}, st);
+}
+
+cudaError_t launch_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
+                                         int kv_stride, const uint16_t *cos_t, const uint16_t *sin_t, int table_rows,
+                                         uint16_t *kc, uint16_t *vc, const int32_t *lengths, uint16_t *out, int batch,
+                                         int heads, int kvh, int hd, int max_pos, float scale, cudaStream_t st) {
+  RopeAppend ra;
+  ra.k_new = reinterpret_cast<const __half *>(k_new);
+  ra.v_new = reinterpret_cast<const __half *>(v_new);
+  ra.kv_stride = kv_stride;
+  ra.cos_t = reinterpret_cast<const __half *>(cos_t);
+  ra.sin_t = reinterpret_cast<const __half *>(sin_t);
+  ra.table_rows = table_rows;
+  return launch_attention(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, hd, max_pos, scale, ra, st);
 }
 
 cudaError_t launch_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,

@@ -38,6 +38,7 @@ SIGNATURES = {
     'lb_linear': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_path': ([_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_select': ([_I, _I, _I, _I, _I, _I], _I),
+    'lb_attention_decode_rope': ([_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P], _I),
     'lb_linear_stacked': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _S, _P], _I),
     'lb_rmsnorm': ([_P, _P, _P, _P, _P, _I, _I, _F, _P], _I),
     'lb_rope': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),

@@ -403,15 +403,23 @@ class FrozenSmolLayer(torch.nn.Module):
         cfg = self.config
         b = h.shape[0]
         normed = self.norm(h, 'input_layernorm.weight') if normed is None else normed
-        q, k, v = self._qkv(normed, lengths, self._rope())
+        qkv = self._stacked('qkv', normed)
+        if qkv is not None:
+            nq, nk, _ = self._stacks['qkv']['widths']
+            q, k, v = qkv[:, :nq], qkv[:, nq:nq + nk], qkv[:, nq + nk:]
+        else:
+            q = self.linear('self_attn.q_proj.weight', normed)
+            k = self.linear('self_attn.k_proj.weight', normed)
+            v = self.linear('self_attn.v_proj.weight', normed)
         L = rt.lib()
         st = rt.stream_ptr(h.device)
-        rt.check(L.lb_kv_append(rt.ptr(k), rt.ptr(v), k.stride(0), rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), b,
-                                cfg.kv_heads, cfg.head_dim, self.max_positions, st), 'lb_kv_append')
+        cos, sin = self._rope()
         attn = torch.empty(b, cfg.heads * cfg.head_dim, dtype=torch.float16, device=h.device)
-        rt.check(L.lb_attention_decode(rt.ptr(q), q.stride(0), rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths), rt.ptr(attn),
-                                       b, cfg.heads, cfg.kv_heads, cfg.head_dim, self.max_positions,
-                                       1.0 / cfg.head_dim ** 0.5, None, 0, st), 'lb_attention_decode')
+        # RoPE of q / k at lengths[b], KV append and attention in one launch
+        rt.check(L.lb_attention_decode_rope(rt.ptr(q), q.stride(0), rt.ptr(k), rt.ptr(v), k.stride(0), rt.ptr(cos),
+                                            rt.ptr(sin), cos.shape[0], rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths),
+                                            rt.ptr(attn), b, cfg.heads, cfg.kv_heads, cfg.head_dim, self.max_positions,
+                                            1.0 / cfg.head_dim ** 0.5, st), 'lb_attention_decode_rope')
         o = self.linear('self_attn.o_proj.weight', attn)
         h1 = torch.empty_like(h)
         normed = self.norm(o, 'post_attention_layernorm.weight', residual=h, residual_out=h1)
