@@ -112,14 +112,16 @@ int lb_linear_select(int fmt, int group, int m, int n, int k, int rank);
  * and their corrections as one block-diagonal correction of the summed rank (<= 128):
  * down = [V_1; V_2; ...] ([rank, K]), up [N, rank] with each linear's U in its own
  * column block and zeros elsewhere, so every output equals the separate call's
- * staging exactly.  residual (optional, [M, N]) is added last, y = half(y + residual):
+ * staging exactly.  z (optional, [M, rank rounded up to 32], zero past the rank) is the
+ * correction projection already computed by lb_rmsnorm_project / lb_silu_mul_project;
+ * it replaces down.  residual (optional, [M, N]) is added last, y = half(y + residual):
  * the residual add of torch_npu_smollm.py:192 fused into the down projection.
  * Workspace: lb_linear_workspace_bytes(fmt, group, m, n, k, rank).  LB_ERR_UNSUPPORTED
  * when the problem is not a decode GEMV (M > 64, unaligned rows or pointers). */
 int lb_linear_stacked(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                      const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
-                      const uint16_t *bias, const uint16_t *residual, uint16_t *y, void *workspace,
-                      size_t workspace_bytes, void *stream);
+                      const uint16_t *scales, const uint16_t *down, const uint16_t *up,
+                      const uint16_t *z, int rank, const uint16_t *bias, const uint16_t *residual,
+                      uint16_t *y, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Allocation-free decode GEMV.  No counterpart in the reference (its linear runs inside
@@ -190,6 +192,17 @@ int lb_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_
  * column blocks of one [rows, 2F] buffer (row stride in elements). */
 int lb_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows,
                 int cols, void *stream);
+/* lb_rmsnorm / lb_silu_mul fused with the correction projection of the linear that
+ * consumes their output: z[r, c] = half(sum_k out[r, k] down[c, k]) for c < rank, zero
+ * up to the row stride (rank rounded up to 32).  No single reference call: the
+ * reference computes x V^T inside each corrected linear (torch_npu_smollm.py:160-163);
+ * the value is the same projection of the same fp16 row.  down / z null: plain op. */
+int lb_rmsnorm_project(const uint16_t *x, const uint16_t *residual, uint16_t *residual_out,
+                       const uint16_t *gamma, uint16_t *out, int rows, int dim, float eps,
+                       const uint16_t *down, int rank, uint16_t *z, void *stream);
+int lb_silu_mul_project(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out,
+                        int rows, int cols, const uint16_t *down, int rank, uint16_t *z,
+                        void *stream);
 /* out[r] = half(a[r] + b[r]) elementwise (residual adds, torch_npu_smollm.py:184,192). */
 int lb_add(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t count, void *stream);
 /* rows of a fp16 table gathered by int64 ids (torch_npu_smollm_io.py:45-50). */

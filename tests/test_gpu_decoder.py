@@ -221,3 +221,43 @@ def test_fused_rope_append_attention_equals_separate_calls(heads, kv, b):
     torch.cuda.synchronize()
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
     assert torch.equal(out1, out2)
+
+
+@pytest.mark.parametrize('rows,dim,rank', [(1, 576, 96), (64, 960, 64), (3, 2048, 32), (5, 192, 0)])
+def test_row_project_ops_equal_separate_ops(rows, dim, rank):
+    """lb_rmsnorm_project / lb_silu_mul_project write the same rows as lb_rmsnorm /
+    lb_silu_mul (bitwise) and z = half(row . V^T) of those rows (fp32 sums of exact fp16
+    products, so within one fp16 rounding of the fp64 projection), zero past the rank."""
+    import lowbit_runtime as rt
+    L, st = rt.lib(), rt.stream_ptr()
+    gen = torch.Generator().manual_seed(rows * dim + rank)
+    x = torch.randn(rows, dim, generator=gen).half().cuda()
+    res = torch.randn(rows, dim, generator=gen).half().cuda()
+    gamma = (1 + 0.1 * torch.randn(dim, generator=gen)).half().cuda()
+    down = (torch.randn(rank, dim, generator=gen) * 0.05).half().cuda() if rank else None
+    zs = max(32, (rank + 31) // 32 * 32)
+    # RMSNorm with residual
+    ref_out, ref_res = torch.empty_like(x), torch.empty_like(x)
+    rt.check(L.lb_rmsnorm(rt.ptr(x), rt.ptr(res), rt.ptr(ref_res), rt.ptr(gamma), rt.ptr(ref_out), rows, dim, 1e-5, st),
+             'lb_rmsnorm')
+    out, res_out = torch.empty_like(x), torch.empty_like(x)
+    z = torch.full((rows, zs), 7.0, dtype=torch.float16, device='cuda') if rank else None
+    rt.check(L.lb_rmsnorm_project(rt.ptr(x), rt.ptr(res), rt.ptr(res_out), rt.ptr(gamma), rt.ptr(out), rows, dim, 1e-5,
+                                  rt.ptr(down), rank, rt.ptr(z), st), 'lb_rmsnorm_project')
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out) and torch.equal(res_out, ref_res)
+    if rank:
+        exact = (out.double() @ down.double().t())
+        assert float((z[:, :rank].double() - exact).abs().max()) <= 2 ** -10 * float(exact.abs().max()) + 1e-3
+        assert int(z[:, rank:].abs().max().item() if zs > rank else 0) == 0
+    # SiLU-mul on column blocks of one [rows, 2 dim] buffer
+    gu = torch.randn(rows, 2 * dim, generator=gen).half().cuda()
+    ref_act, act = torch.empty_like(x), torch.empty_like(x)
+    rt.check(L.lb_silu_mul(rt.ptr(gu), rt.ptr(gu[:, dim:]), 2 * dim, rt.ptr(ref_act), rows, dim, st), 'lb_silu_mul')
+    rt.check(L.lb_silu_mul_project(rt.ptr(gu), rt.ptr(gu[:, dim:]), 2 * dim, rt.ptr(act), rows, dim, rt.ptr(down), rank,
+                                   rt.ptr(z), st), 'lb_silu_mul_project')
+    torch.cuda.synchronize()
+    assert torch.equal(act, ref_act)
+    if rank:
+        exact = (act.double() @ down.double().t())
+        assert float((z[:, :rank].double() - exact).abs().max()) <= 2 ** -10 * float(exact.abs().max()) + 1e-3

@@ -42,6 +42,9 @@ cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint
 cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *kc, uint16_t *vc,
                              const int32_t *lengths, int batch, int kvh, int hd, int max_pos, cudaStream_t st);
 size_t attention_smem(int heads, int kvh, int max_pos);
+cudaError_t launch_row_project(int mode, const uint16_t *x, const uint16_t *res, uint16_t *res_out,
+                               const uint16_t *gamma, uint16_t *out, int rows, int dim, int in_stride, float eps,
+                               const uint16_t *v, int rank, uint16_t *z, cudaStream_t st);
 cudaError_t launch_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
                                          int kv_stride, const uint16_t *cos_t, const uint16_t *sin_t, int table_rows,
                                          uint16_t *kc, uint16_t *vc, const int32_t *lengths, uint16_t *out, int batch,
@@ -303,18 +306,20 @@ int lb_linear(int fmt, int group, int m, int n, int k, const uint16_t *x, const 
 }
 
 int lb_linear_stacked(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
-                      const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank, const uint16_t *bias,
-                      const uint16_t *residual, uint16_t *y, void *workspace, size_t workspace_bytes, void *stream) {
+                      const uint16_t *scales, const uint16_t *down, const uint16_t *up, const uint16_t *z_in,
+                      int rank, const uint16_t *bias, const uint16_t *residual, uint16_t *y, void *workspace,
+                      size_t workspace_bytes, void *stream) {
   if (injected("lb_linear_stacked")) return LB_ERR_INJECTED;
   if (!valid_format(fmt) || m < 1 || n < 1 || k < 1 || !x || !codes || !y) return LB_ERR_INVALID_ARGUMENT;
   if (fmt != LB_FMT_FP16 && (!scales || group < 1 || group > k || k % group)) return LB_ERR_INVALID_ARGUMENT;
-  if ((down == nullptr) != (up == nullptr)) return LB_ERR_INVALID_ARGUMENT;
-  if (down && (rank < 1 || rank > 128 || rank > k)) return LB_ERR_INVALID_ARGUMENT;
+  if (z_in && (down || !up)) return LB_ERR_INVALID_ARGUMENT;   // a given z replaces the projection
+  if (!z_in && (down == nullptr) != (up == nullptr)) return LB_ERR_INVALID_ARGUMENT;
+  if (up && (rank < 1 || rank > 128 || rank > k)) return LB_ERR_INVALID_ARGUMENT;
   if (int64_t(m) * k > (int64_t(1) << 40) || int64_t(n) * k > (int64_t(1) << 40)) return LB_ERR_INVALID_ARGUMENT;
-  if (!down) rank = 0;
+  if (!up) rank = 0;
   if (fmt == LB_FMT_FP16) group = k;
   if (!gemv_supported(fmt, group, m, n, k) || !aligned16(x) || !aligned16(codes) || !aligned16(y) ||
-      !aligned16(workspace) || (down && (!aligned16(down) || !aligned16(up))))
+      !aligned16(workspace) || (down && !aligned16(down)) || (up && !aligned16(up)) || (z_in && !aligned16(z_in)))
     return LB_ERR_UNSUPPORTED;
   const size_t need = kHeader + z_bytes(m, rank) + align256(gemv_workspace_bytes(fmt, m, n, k));
   if (!workspace || workspace_bytes < need) return LB_ERR_WORKSPACE;
@@ -328,9 +333,13 @@ int lb_linear_stacked(int fmt, int group, int m, int n, int k, const uint16_t *x
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   const int zs = (rank + 31) / 32 * 32;
-  uint16_t *z = rank > 0 ? reinterpret_cast<uint16_t *>(ws + kHeader) : nullptr;
+  const uint16_t *z = z_in;
   cudaError_t e = cudaSuccess;
-  if (z) e = launch_lowrank_project(m, k, rank, zs, x, down, z, st);
+  if (rank > 0 && !z_in) {
+    uint16_t *zw = reinterpret_cast<uint16_t *>(ws + kHeader);
+    e = launch_lowrank_project(m, k, rank, zs, x, down, zw, st);
+    z = zw;
+  }
   if (e == cudaSuccess)
     e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, zs, up, rank, bias, residual, y,
                     ws + kHeader + z_bytes(m, rank), reinterpret_cast<int *>(ws + kCounterOffset), st);
@@ -415,6 +424,39 @@ int lb_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_
   return cuda_status(launch_attention_decode_rope(q, q_stride, k_new, v_new, kv_stride, cos_table, sin_table,
                                                   table_rows, k_cache, v_cache, lengths, out, batch, heads, kv_heads,
                                                   head_dim, max_pos, scale, static_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+int row_project(int mode, const uint16_t *x, const uint16_t *res, uint16_t *res_out, const uint16_t *gamma,
+                uint16_t *out, int rows, int dim, int in_stride, float eps, const uint16_t *down, int rank, uint16_t *z,
+                void *stream) {
+  if (!x || !out || rows < 1 || dim < 8 || dim % 8 || dim > 16384) return LB_ERR_INVALID_ARGUMENT;
+  if ((down == nullptr) != (z == nullptr) || (down && (rank < 1 || rank > 128))) return LB_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(out) || (res && !aligned16(res)) || (res_out && !aligned16(res_out)) ||
+      (gamma && !aligned16(gamma)) || (down && (!aligned16(down) || !aligned16(z))))
+    return LB_ERR_INVALID_ARGUMENT;
+  return cuda_status(launch_row_project(mode, x, res, res_out, gamma, out, rows, dim, in_stride, eps, down, rank, z,
+                                        static_cast<cudaStream_t>(stream)));
+}
+}  // namespace
+
+int lb_rmsnorm_project(const uint16_t *x, const uint16_t *residual, uint16_t *residual_out, const uint16_t *gamma,
+                       uint16_t *out, int rows, int dim, float eps, const uint16_t *down, int rank, uint16_t *z,
+                       void *stream) {
+  if (injected("lb_rmsnorm_project")) return LB_ERR_INJECTED;
+  if (!gamma || !(eps >= 0.f)) return LB_ERR_INVALID_ARGUMENT;
+  const size_t b = size_t(rows) * dim * 2;
+  if (rows > 0 && dim > 0 && (overlaps(out, b, x, b) || (residual && overlaps(out, b, residual, b)) ||
+                              (residual_out && overlaps(out, b, residual_out, b))))
+    return LB_ERR_ALIAS;
+  return row_project(0, x, residual, residual_out, gamma, out, rows, dim, dim, eps, down, rank, z, stream);
+}
+
+int lb_silu_mul_project(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,
+                        const uint16_t *down, int rank, uint16_t *z, void *stream) {
+  if (injected("lb_silu_mul_project")) return LB_ERR_INJECTED;
+  if (!up || in_stride < cols || in_stride % 8 || !aligned16(up)) return LB_ERR_INVALID_ARGUMENT;
+  return row_project(1, gate, up, nullptr, nullptr, out, rows, cols, in_stride, 0.f, down, rank, z, stream);
 }
 
 int lb_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,

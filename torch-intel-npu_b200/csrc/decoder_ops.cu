@@ -321,6 +321,114 @@ __global__ void silu_mul_kernel(const __half *__restrict__ gate, const __half *_
   }
 }
 
+// A row producer fused with the correction projection of the linear that consumes it:
+// CTA (row, j) builds the produced fp16 row in shared memory -- RMSNorm with the optional
+// residual add (MODE 0, same staging as rmsnorm_kernel) or half(half(silu(g)) * u)
+// (MODE 1, as silu_mul_kernel) -- the j == 0 CTA stores it (and the new hidden state),
+// and every CTA computes z[row, 8j + w] = half(sum_k row_k V[8j + w, k]) for its 8 columns,
+// one per warp (zero past the rank): the projection the GEMV epilogue then applies.
+struct RowProjParams {
+  const __half *x, *res;   // MODE 0: x, residual (or null); MODE 1: gate, up
+  __half *res_out;         // MODE 0: half(x + residual), or null
+  const __half *gamma;     // MODE 0
+  __half *out;             // produced row [rows, dim]
+  int dim, in_stride;      // MODE 1: gate / up row stride
+  float eps;
+  const __half *v;         // [rank, dim] or null
+  int rank, zs;            // z row stride (rank rounded up to 32)
+  __half *z;               // [rows, zs]
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(256) row_project_kernel(const RowProjParams p) {
+  extern __shared__ __align__(16) __half rowbuf[];   // [dim]
+  __shared__ float sh[32];
+  pdl_launch();
+  pdl_wait();
+  const int64_t r = blockIdx.x;
+  const bool store = blockIdx.y == 0;
+  const int nvec = p.dim / 8;
+  if constexpr (MODE == 0) {
+    constexpr int MAXV = 8;
+    float v[MAXV * 8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        uint4 a = *reinterpret_cast<const uint4 *>(p.x + r * p.dim + c * 8);
+        const __half *ah = reinterpret_cast<const __half *>(&a);
+        if (p.res) {
+          uint4 b = *reinterpret_cast<const uint4 *>(p.res + r * p.dim + c * 8);
+          const __half *bh = reinterpret_cast<const __half *>(&b);
+          uint4 h;
+          __half *hh = reinterpret_cast<__half *>(&h);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) hh[j] = __float2half_rn(__half2float(ah[j]) + __half2float(bh[j]));
+          if (p.res_out && store) *reinterpret_cast<uint4 *>(p.res_out + r * p.dim + c * 8) = h;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i * 8 + j] = __half2float(hh[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i * 8 + j] = __half2float(ah[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(v[i * 8 + j], v[i * 8 + j], ss);
+      }
+    }
+    const float total = block_sum(ss, sh);
+    const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, float(p.dim)), p.eps));
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        uint4 g = *reinterpret_cast<const uint4 *>(p.gamma + c * 8);
+        const __half *gh = reinterpret_cast<const __half *>(&g);
+        uint4 o;
+        __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) oh[j] = __hmul(__float2half_rn(__fmul_rn(v[i * 8 + j], inv)), gh[j]);
+        reinterpret_cast<uint4 *>(rowbuf)[c] = o;
+        if (store) *reinterpret_cast<uint4 *>(p.out + r * p.dim + c * 8) = o;
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
+      const uint4 g = *reinterpret_cast<const uint4 *>(p.x + r * p.in_stride + c * 8);
+      const uint4 u = *reinterpret_cast<const uint4 *>(p.res + r * p.in_stride + c * 8);
+      const __half *gh = reinterpret_cast<const __half *>(&g), *uh = reinterpret_cast<const __half *>(&u);
+      uint4 o;
+      __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float gv = __half2float(gh[j]);
+        oh[j] = __hmul(__float2half_rn(__fdiv_rn(gv, 1.f + expf(-gv))), uh[j]);
+      }
+      reinterpret_cast<uint4 *>(rowbuf)[c] = o;
+      if (store) *reinterpret_cast<uint4 *>(p.out + r * p.dim + c * 8) = o;
+    }
+  }
+  if (!p.v) return;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.y * 8 + warp;
+  float acc = 0.f;
+  if (col < p.rank) {
+    const __half *vr = p.v + int64_t(col) * p.dim;
+#pragma unroll 4
+    for (int c = lane; c < nvec; c += 32) {
+      const uint4 a = reinterpret_cast<const uint4 *>(rowbuf)[c];
+      const uint4 b = *reinterpret_cast<const uint4 *>(vr + c * 8);
+      fma2_f16_f32(acc, a.x, b.x);
+      fma2_f16_f32(acc, a.y, b.y);
+      fma2_f16_f32(acc, a.z, b.z);
+      fma2_f16_f32(acc, a.w, b.w);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0 && col < p.zs) p.z[r * p.zs + col] = __float2half_rn(col < p.rank ? acc : 0.f);
+}
+
 __global__ void add_kernel(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ out,
                            int64_t count) {
   pdl_launch();
@@ -391,6 +499,37 @@ cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *res, uint16_t *res
   return launch_k(rmsnorm_kernel, dim3(rows), dim3(threads), 0, st, reinterpret_cast<const __half *>(x),
                   reinterpret_cast<const __half *>(res), reinterpret_cast<__half *>(res_out),
                   reinterpret_cast<const __half *>(gamma), reinterpret_cast<__half *>(out), dim, eps);
+}
+
+// mode 0: RMSNorm (+ residual) rows, mode 1: SiLU-mul rows; z for the following linear.
+cudaError_t launch_row_project(int mode, const uint16_t *x, const uint16_t *res, uint16_t *res_out,
+                               const uint16_t *gamma, uint16_t *out, int rows, int dim, int in_stride, float eps,
+                               const uint16_t *v, int rank, uint16_t *z, cudaStream_t st) {
+  RowProjParams p;
+  p.x = reinterpret_cast<const __half *>(x);
+  p.res = reinterpret_cast<const __half *>(res);
+  p.res_out = reinterpret_cast<__half *>(res_out);
+  p.gamma = reinterpret_cast<const __half *>(gamma);
+  p.out = reinterpret_cast<__half *>(out);
+  p.dim = dim;
+  p.in_stride = in_stride;
+  p.eps = eps;
+  p.v = reinterpret_cast<const __half *>(v);
+  p.rank = v ? rank : 0;
+  p.zs = v ? (rank + 31) / 32 * 32 : 32;
+  p.z = reinterpret_cast<__half *>(z);
+  const dim3 grid(rows, v ? p.zs / 8 : 1);   // 8 z columns (one per warp) per CTA
+  const size_t smem = size_t(dim) * 2;
+  if (mode == 0) {
+    auto kern = row_project_kernel<0>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    return launch_k(kern, grid, dim3(256), smem, st, p);
+  }
+  auto kern = row_project_kernel<1>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return launch_k(kern, grid, dim3(256), smem, st, p);
 }
 
 cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint16_t *cos_t, const uint16_t *sin_t,

@@ -39,7 +39,9 @@ SIGNATURES = {
     'lb_linear_path': ([_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_select': ([_I, _I, _I, _I, _I, _I], _I),
     'lb_attention_decode_rope': ([_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P], _I),
-    'lb_linear_stacked': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _S, _P], _I),
+    'lb_linear_stacked': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _S, _P], _I),
+    'lb_rmsnorm_project': ([_P, _P, _P, _P, _P, _I, _I, _F, _P, _I, _P, _P], _I),
+    'lb_silu_mul_project': ([_P, _P, _I, _P, _I, _I, _P, _I, _P, _P], _I),
     'lb_rmsnorm': ([_P, _P, _P, _P, _P, _I, _I, _F, _P], _I),
     'lb_rope': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     'lb_kv_append': ([_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _P], _I),
@@ -203,20 +205,22 @@ def linear(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, ou
     return y
 
 
-def linear_stacked(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, residual=None, out=None):
+def linear_stacked(x, fmt, group, n, codes, scales, *, down=None, up=None, z=None, bias=None, residual=None, out=None):
     """One decode-GEMV launch over several stacked linears (lb_linear_stacked): codes /
     scales / bias are the row-wise concatenation, down / up the block-diagonal stack of
-    their corrections (rank <= 128); residual [M, N] is added last."""
+    their corrections (rank <= 128); z, when given, is their projection already computed
+    (it replaces down); residual [M, N] is added last."""
     L = require_cuda()
     x = _contig_cuda(x, 'x', torch.float16)
     m, k = x.shape
-    rank = 0 if down is None else down.shape[0]
+    rank = 0 if up is None else up.shape[1]
     y = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=x.device)
     if residual is not None:
         residual = _contig_cuda(residual, 'residual', torch.float16)
     ws = Workspace.get(L.lb_linear_workspace_bytes(LB_FMT[fmt], group, m, n, k, rank), x.device)
-    status = L.lb_linear_stacked(LB_FMT[fmt], group, m, n, k, ptr(x), ptr(codes), ptr(scales), ptr(down), ptr(up),
-                                 rank, ptr(bias), ptr(residual), ptr(y), ptr(ws), ws.numel(), stream_ptr(x.device))
+    status = L.lb_linear_stacked(LB_FMT[fmt], group, m, n, k, ptr(x), ptr(codes), ptr(scales),
+                                 ptr(down if z is None else None), ptr(up), ptr(z), rank, ptr(bias), ptr(residual),
+                                 ptr(y), ptr(ws), ws.numel(), stream_ptr(x.device))
     check(status, 'lb_linear_stacked')
     return y
 

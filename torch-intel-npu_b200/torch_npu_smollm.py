@@ -33,6 +33,7 @@ from torch_npu_lowbit_correction import LowRankCorrection
 
 _STACKS = {'qkv': ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight'),
            'gate_up': ('mlp.gate_proj.weight', 'mlp.up_proj.weight')}
+_FUSE_Z_ROWS = 16
 _PROJECTIONS = ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight',
                 'self_attn.o_proj.weight', 'mlp.gate_proj.weight', 'mlp.up_proj.weight', 'mlp.down_proj.weight')
 _NORMS = ('input_layernorm.weight', 'post_attention_layernorm.weight')
@@ -399,20 +400,33 @@ class FrozenSmolLayer(torch.nn.Module):
         return out.view(b, 1, -1), SmolKVCache(self._owner, cache._sequence, store, cache.length + 1)
 
     def decode_step(self, h, k_cache, v_cache, lengths, normed=None):
-        """One token for every sequence: h [B, d] -> output [B, d]; writes K/V at lengths[b]."""
+        """One token for every sequence: h [B, d] -> output [B, d]; writes K/V at lengths[b].
+
+        Decode batches (<= 64 rows) run 9 launches per layer: RMSNorm + z(q|k|v), the
+        stacked q|k|v GEMV, RoPE + KV append + attention, z(o) + o GEMV, RMSNorm with the
+        residual + z(gate|up), the stacked gate|up GEMV, SiLU-mul + z(down), and the down
+        GEMV with the residual add in its epilogue."""
         cfg = self.config
         b = h.shape[0]
-        normed = self.norm(h, 'input_layernorm.weight') if normed is None else normed
-        qkv = self._stacked('qkv', normed)
-        if qkv is not None:
-            nq, nk, _ = self._stacks['qkv']['widths']
+        L = rt.lib()
+        st = rt.stream_ptr(h.device)
+        qs = self._stack_for('qkv', b)
+        # z fused into the row producers only for small batches: from 16 rows on, the
+        # projection kernel that shares each V row across 8 activation rows is faster
+        fuse_z = b <= _FUSE_Z_ROWS
+        z = None
+        if normed is None:
+            normed, z = self._norm_project(h, 'input_layernorm.weight',
+                                           None if qs is None or not fuse_z else qs['down'])
+        if qs is not None:
+            qkv = rt.linear_stacked(normed, qs['fmt'], qs['group'], qs['n'], qs['codes'], qs['scales'],
+                                    down=qs['down'] if z is None else None, up=qs['up'], z=z)
+            nq, nk, _ = qs['widths']
             q, k, v = qkv[:, :nq], qkv[:, nq:nq + nk], qkv[:, nq + nk:]
         else:
             q = self.linear('self_attn.q_proj.weight', normed)
             k = self.linear('self_attn.k_proj.weight', normed)
             v = self.linear('self_attn.v_proj.weight', normed)
-        L = rt.lib()
-        st = rt.stream_ptr(h.device)
         cos, sin = self._rope()
         attn = torch.empty(b, cfg.heads * cfg.head_dim, dtype=torch.float16, device=h.device)
         # RoPE of q / k at lengths[b], KV append and attention in one launch
@@ -422,13 +436,55 @@ class FrozenSmolLayer(torch.nn.Module):
                                             1.0 / cfg.head_dim ** 0.5, st), 'lb_attention_decode_rope')
         o = self.linear('self_attn.o_proj.weight', attn)
         h1 = torch.empty_like(h)
-        normed = self.norm(o, 'post_attention_layernorm.weight', residual=h, residual_out=h1)
-        down, fused = self._ffn(normed, residual=h1)
-        if fused:
-            return down
+        gs = self._stack_for('gate_up', b)
+        normed, z = self._norm_project(o, 'post_attention_layernorm.weight',
+                                       None if gs is None or not fuse_z else gs['down'], residual=h, residual_out=h1)
+        if gs is not None:
+            gu = rt.linear_stacked(normed, gs['fmt'], gs['group'], gs['n'], gs['codes'], gs['scales'],
+                                   down=gs['down'] if z is None else None, up=gs['up'], z=z)
+            ni = gs['widths'][0]
+            gate, up = gu[:, :ni], gu[:, ni:]
+        else:
+            gate = self.linear('mlp.gate_proj.weight', normed)
+            up = self.linear('mlp.up_proj.weight', normed)
+        dp = self._proj['mlp.down_proj.weight']
+        fused_down = self._tp is None and rt.linear_select(dp['fmt'], dp['group'], b, dp['n'], dp['k']) == 'gemv'
+        rows, cols = gate.shape
+        act = torch.empty(rows, cols, dtype=torch.float16, device=h.device)
+        zd = None
+        if fused_down and fuse_z and dp['down'] is not None:
+            zd = torch.empty(rows, (dp['down'].shape[0] + 31) // 32 * 32, dtype=torch.float16, device=h.device)
+        rt.check(L.lb_silu_mul_project(rt.ptr(gate), rt.ptr(up), gate.stride(0), rt.ptr(act), rows, cols,
+                                       rt.ptr(dp['down'] if zd is not None else None),
+                                       0 if zd is None else dp['down'].shape[0], rt.ptr(zd), st), 'lb_silu_mul_project')
+        if fused_down:
+            return rt.linear_stacked(act, dp['fmt'], dp['group'], dp['n'], dp['codes'], dp['scales'],
+                                     down=dp['down'] if zd is None else None, up=dp['up'], z=zd, residual=h1)
+        down = self.linear('mlp.down_proj.weight', act)
         out = torch.empty_like(h)
         rt.check(L.lb_add(rt.ptr(h1), rt.ptr(down), rt.ptr(out), out.numel(), st), 'lb_add')
         return out
+
+    def _stack_for(self, key, rows):
+        """The stacked projection when its single decode-GEMV launch applies, else None."""
+        st = self._stacks.get(key)
+        if st is None or rt.linear_select(st['fmt'], st['group'], rows, st['n'], st['k']) != 'gemv':
+            return None
+        return st
+
+    def _norm_project(self, x, name, down, residual=None, residual_out=None):
+        """RMSNorm (+ residual) of x and, when ``down`` is given, z = half(normed . down^T)
+        for the linear that reads it (lb_rmsnorm_project): (normed, z or None)."""
+        rows, d = x.shape
+        out = torch.empty(rows, d, dtype=torch.float16, device=x.device)
+        z = None
+        if down is not None:
+            z = torch.empty(rows, (down.shape[0] + 31) // 32 * 32, dtype=torch.float16, device=x.device)
+        rt.check(rt.lib().lb_rmsnorm_project(rt.ptr(x), rt.ptr(residual), rt.ptr(residual_out), rt.ptr(self._norm[name]),
+                                             rt.ptr(out), rows, d, self.config.eps, rt.ptr(down),
+                                             0 if down is None else down.shape[0], rt.ptr(z), rt.stream_ptr(x.device)),
+                 'lb_rmsnorm_project')
+        return out, z
 
 
 class FrozenSmolStack(torch.nn.Module):
