@@ -50,12 +50,16 @@ struct GemvParams {
   float *partial;        // [splits, m, n] fp32 when gridDim.y > 1
   int *counters;         // [gridDim.x] arrival counters (zero between calls)
   int prefetch;
+  int gshift;            // log2(group / chunk elements) when that is a power of two, else -1
 };
 
 // NCOL = 8-column groups of activation rows (M <= 8 NCOL).  Up to 16 columns the x pairs
 // of a round are loaded up front and each warp may hold two row groups with two
 // accumulator chains; from 32 columns on (batched decode) a warp holds one row group and
 // its dequantized fragments are reused across the column groups while x is streamed.
+// Reduction buffer: [warps_k][rows_cta][LDC] floats, warps_k * rows_cta <= 128 * row groups.
+template <int NCOL> constexpr int red_words() { return 128 * (NCOL > 2 ? 1 : kMaxRowGroups) * 8 * NCOL; }
+
 template <int FMT, int NCOL>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   constexpr int E = FmtTraits<FMT>::E;
@@ -68,7 +72,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   constexpr int LDC = 8 * NCOL;                   // reduction row stride (columns)
   extern __shared__ __align__(16) uint32_t smem[];
   float *red = reinterpret_cast<float *>(smem);                        // [warps_k][rows_cta][LDC]
-  uint32_t *lut = smem + kWarps * 64 * 16;
+  uint32_t *lut = smem + red_words<NCOL>();
   __shared__ int s_last;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -86,21 +90,25 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   const int groups_per_row = FMT == LB_FMT_FP16 ? 1 : p.k / p.group;
   const bool per_row_scale = FMT == LB_FMT_INT8 && p.group == p.k;
   // One round of weight loads: two K blocks x rpw row groups x rows g / g+8, with scales.
+  // Per-lane bases of row g (row g+8 and the next row group are fixed offsets from it).
+  const uint8_t *code_base = p.codes + int64_t(wrow0 + g) * row_bytes + 16 * t;
+  const __half *scale_base = p.scales + int64_t(wrow0 + g) * groups_per_row;
   auto load_round = [&](int kbA, uint4 (&q)[2][RG][2], __half2 (&s2)[2][RG][2]) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int kb = kbA + u * p.warps_k;
       const int chunk = kb * 4 + t;
       const bool kvalid = kb < kb1 && chunk < chunks;
+      const int gi = p.gshift >= 0 ? chunk >> p.gshift : (chunk * E) / p.group;
 #pragma unroll
       for (int r = 0; r < RG; ++r) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int row = wrow0 + 16 * r + g + 8 * h;
           const bool ok = r < p.rpw && kvalid && row < p.n;
-          q[u][r][h] = ok ? ldg_nc_v4(p.codes + int64_t(row) * row_bytes + int64_t(chunk) * 16) : make_uint4(0, 0, 0, 0);
+          q[u][r][h] = ok ? ldg_nc_v4(code_base + (16 * r + 8 * h) * row_bytes + int64_t(kb) * 64) : make_uint4(0, 0, 0, 0);
           if constexpr (FMT != LB_FMT_FP16) {
-            const __half sc = (ok && !per_row_scale) ? p.scales[int64_t(row) * groups_per_row + (chunk * E) / p.group]
+            const __half sc = (ok && !per_row_scale) ? scale_base[(16 * r + 8 * h) * groups_per_row + gi]
                                                      : __float2half(1.f);
             s2[u][r][h] = __halves2half2(sc, sc);
           } else {
@@ -522,8 +530,10 @@ size_t gemv_workspace_bytes(int fmt, int m, int n, int k) {
 }
 
 template <int FMT, int NCOL>
-static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t smem, cudaStream_t st) {
+static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t, cudaStream_t st) {
   auto kern = gemv_kernel<FMT, NCOL>;
+  size_t smem = size_t(red_words<NCOL>()) * sizeof(float);
+  if (FMT == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   return launch_k(kern, grid, dim3(32 * kWarps), smem, st, p);
@@ -582,6 +592,12 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
     p.counters = counters;
   }
   p.prefetch = gemv_prefetch_mode();
+  p.gshift = -1;
+  {
+    const int cpg = p.group / gemv_elems(fmt);   // chunks per scale group
+    if (fmt != LB_FMT_FP16 && p.group % gemv_elems(fmt) == 0 && cpg > 0 && (cpg & (cpg - 1)) == 0)
+      for (p.gshift = 0; (1 << p.gshift) < cpg; ++p.gshift) {}
+  }
   const int ncol = m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8));
   size_t smem = size_t(kWarps) * 64 * 16 * sizeof(float);
   if (fmt == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
