@@ -487,9 +487,9 @@ int gemv_prefetch_mode() {
 struct GemvPlan { int warps_k, rpw, splits, kb_per_split, ctas_x; };
 
 // Work split over 16-row groups x 64-byte K blocks.  A rough time model: resident CTAs
-// (2 per SM) must keep ~6 MB of 128-bit loads in flight to cover HBM latency, every
-// extra wave repeats the latency, and a cross-CTA K split adds a reduction pass.
-// LOWBIT_GEMV_PLAN="warps_k,rpw,splits" overrides the choice (tuning).
+// must keep ~6 MB of 128-bit loads in flight to cover HBM latency, every extra wave and
+// every round of loads per warp repeats the latency, and a cross-CTA K split adds a
+// reduction pass.  LOWBIT_GEMV_PLAN="warps_k,rpw,splits" overrides the choice (tuning).
 static GemvPlan gemv_plan(int fmt, int m, int n, int k) {
   const int e = gemv_elems(fmt);
   const int kblocks = (k / e + 3) / 4;
@@ -511,11 +511,15 @@ static GemvPlan gemv_plan(int fmt, int m, int n, int k) {
         const int ctas = ((groups + wr * rpw - 1) / (wr * rpw)) * ((kblocks + kbs - 1) / kbs);
         const int loads = rpw * ((kbs + wk - 1) / wk);          // 1 KB warp loads per warp
         const int rounds = ((kbs + wk - 1) / wk + 1) / 2;       // two K blocks per round
-        const double resident = ctas < 2 * 148 ? ctas : 2 * 148;
+        // CTAs resident per SM: the 2-column kernel holds more than 128 registers
+        const int per_sm = (m > 8 && m <= 16) ? 1 : 2;
+        const double resident = ctas < per_sm * 148 ? ctas : per_sm * 148;
         const double fill = resident * kWarps * loads * 1024.0 / 6.0e6;
-        const int waves = (ctas + 2 * 148 - 1) / (2 * 148);
-        double cost = waves * (0.6 * rounds + 0.4 + 0.05 * loads) / (fill < 1.0 ? fill : 1.0);
-        if (sp > 1) cost += 0.5 + (m > 16 ? m / 16.0 : 0.0);   // the last CTA's partial sums grow with M
+        const int waves = (ctas + per_sm * 148 - 1) / (per_sm * 148);
+        // small problems are latency-bound: below half the in-flight target more CTAs do
+        // not shorten a round (fitted to B200 measurements of the candidate plans)
+        double cost = waves * (0.6 * rounds + 0.4 + 0.05 * loads) / (fill < 1.0 ? (fill > 0.5 ? fill : 0.5) : 1.0);
+        if (sp > 1) cost += 1.5 + (m > 16 ? m / 16.0 : 0.0);   // partial sums grow with M
         if (cost < best_cost) { best_cost = cost; best = {wk, rpw, (kblocks + kbs - 1) / kbs, kbs, (groups + wr * rpw - 1) / (wr * rpw)}; }
       }
     }
