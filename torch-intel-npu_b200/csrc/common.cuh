@@ -1,5 +1,7 @@
 // Shared device helpers for the low-bit kernels (sm_100a only).
 #pragma once
+#include <mutex>
+#include <unordered_map>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -170,6 +172,23 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // Host-side launch helpers.
 namespace lowbit_host {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) is a driver round trip: issue it once
+// per (kernel, device) and whenever a larger size is requested.
+inline cudaError_t ensure_dyn_smem(const void *func, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t key = (uint64_t(reinterpret_cast<uintptr_t>(func)) << 6) ^ uint64_t(dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
 bool pdl_enabled();  // defined in abi.cu (env LOWBIT_PDL, default on)
 
 // cudaLaunchKernelEx with programmatic dependent launch when enabled: every kernel of

@@ -522,12 +522,12 @@ cudaError_t launch_row_project(int mode, const uint16_t *x, const uint16_t *res,
   const size_t smem = size_t(dim) * 2;
   if (mode == 0) {
     auto kern = row_project_kernel<0>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), int(smem));
     if (e != cudaSuccess) return e;
     return launch_k(kern, grid, dim3(256), smem, st, p);
   }
   auto kern = row_project_kernel<1>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), int(smem));
   if (e != cudaSuccess) return e;
   return launch_k(kern, grid, dim3(256), smem, st, p);
 }
@@ -556,7 +556,7 @@ static cudaError_t launch_attention_rep(const uint16_t *q, int q_stride, uint16_
                                         const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh,
                                         int max_pos, float scale, size_t smem, const RopeAppend &ra, cudaStream_t st) {
   auto kern = attention_decode_kernel<64, REP>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), int(smem));
   if (e != cudaSuccess) return e;
   return launch_k(kern, dim3(batch * kvh), dim3(256), smem, st, reinterpret_cast<const __half *>(q), q_stride,
                   reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), lengths,

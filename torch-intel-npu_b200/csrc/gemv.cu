@@ -490,7 +490,27 @@ struct GemvPlan { int warps_k, rpw, splits, kb_per_split, ctas_x; };
 // must keep ~6 MB of 128-bit loads in flight to cover HBM latency, every extra wave and
 // every round of loads per warp repeats the latency, and a cross-CTA K split adds a
 // reduction pass.  LOWBIT_GEMV_PLAN="warps_k,rpw,splits" overrides the choice (tuning).
+static GemvPlan gemv_plan_search(int fmt, int m, int n, int k);
+
+// Plans are pure functions of the problem: cached per (format, M, N, K) unless a plan is
+// forced through the environment.
 static GemvPlan gemv_plan(int fmt, int m, int n, int k) {
+  if (getenv("LOWBIT_GEMV_PLAN")) return gemv_plan_search(fmt, m, n, k);
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, GemvPlan> cache;
+  const uint64_t key = (uint64_t(fmt) << 60) ^ (uint64_t(m) << 48) ^ (uint64_t(uint32_t(n)) << 24) ^ uint64_t(uint32_t(k));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const GemvPlan pl = gemv_plan_search(fmt, m, n, k);
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() < 65536) cache.emplace(key, pl);
+  return pl;
+}
+
+static GemvPlan gemv_plan_search(int fmt, int m, int n, int k) {
   const int e = gemv_elems(fmt);
   const int kblocks = (k / e + 3) / 4;
   const int groups = (n + 15) / 16;
@@ -538,7 +558,7 @@ static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t, cudaStr
   auto kern = gemv_kernel<FMT, NCOL>;
   size_t smem = size_t(red_words<NCOL>()) * sizeof(float);
   if (FMT == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), int(smem));
   if (e != cudaSuccess) return e;
   return launch_k(kern, grid, dim3(32 * kWarps), smem, st, p);
 }

@@ -458,7 +458,7 @@ static cudaError_t launch_tc_t(const CUtensorMap &w, const CUtensorMap &x, const
                                const TcParams &p, cudaStream_t st) {
   using L = TcLayout<FMT, BM>;
   auto kern = tc_linear_kernel<FMT, BM>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), L::TOTAL);
   if (e != cudaSuccess) return e;
   dim3 grid((p.n + 127) / 128, (p.m + BM - 1) / BM, p.splits);
   return launch_k(kern, grid, dim3(kTcThreads), size_t(L::TOTAL), st, w, x, u, z, p);

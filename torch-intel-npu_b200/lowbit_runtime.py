@@ -10,6 +10,7 @@ There is no CPU fallback: without a CUDA device or without the built library eve
 entry point raises.
 """
 import ctypes
+import functools
 import threading
 from pathlib import Path
 
@@ -80,9 +81,15 @@ def lib():
     return _LIB if _LIB is not None else load_library()
 
 
+_CUDA_OK = False
+
+
 def require_cuda():
-    if not torch.cuda.is_available():
-        raise RuntimeError('The B200 low-bit path requires a CUDA device; there is no CPU fallback')
+    global _CUDA_OK
+    if not _CUDA_OK:
+        if not torch.cuda.is_available():
+            raise RuntimeError('The B200 low-bit path requires a CUDA device; there is no CPU fallback')
+        _CUDA_OK = True
     return lib()
 
 
@@ -126,7 +133,16 @@ class Workspace:
     @classmethod
     def get(cls, nbytes, device=None):
         dev = torch.device('cuda', torch.cuda.current_device() if device is None else torch.device(device).index or 0)
-        key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+        return cls.for_stream(nbytes, dev.index, torch.cuda.current_stream(dev).cuda_stream)
+
+    @classmethod
+    def for_stream(cls, nbytes, index, stream_handle):
+        """The buffer of device ``index`` / stream handle, grown to ``nbytes``."""
+        key = (index, stream_handle)
+        buf = cls._buffers.get(key)
+        if buf is not None and buf.numel() >= nbytes:   # common case: no lock needed to read
+            return buf
+        dev = torch.device('cuda', index)
         with cls._lock:
             buf = cls._buffers.get(key)
             if buf is None or buf.numel() < nbytes:
@@ -191,17 +207,31 @@ def linear_workspace_bytes(fmt, group, m, n, k, rank):
     return lib().lb_linear_workspace_bytes(LB_FMT[fmt], group, m, n, k, rank)
 
 
+@functools.lru_cache(maxsize=4096)
+def _linear_ws_bytes(fmt_id, group, m, n, k, rank):
+    return lib().lb_linear_workspace_bytes(fmt_id, group, m, n, k, rank)
+
+
+def _addr(t):
+    return None if t is None else t.data_ptr()
+
+
 def linear(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, out=None, path='auto'):
     """y = x . deq(W)^T (+ bias) (+ correction) through lb_linear_path."""
     L = require_cuda()
     x = _contig_cuda(x, 'x', torch.float16)
     m, k = x.shape
     rank = 0 if down is None else down.shape[0]
-    y = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=x.device)
-    ws = Workspace.get(L.lb_linear_workspace_bytes(LB_FMT[fmt], group, m, n, k, rank), x.device)
-    status = L.lb_linear_path(PATH[path], LB_FMT[fmt], group, m, n, k, ptr(x), ptr(codes), ptr(scales), ptr(down),
-                              ptr(up), rank, ptr(bias), ptr(y), ptr(ws), ws.numel(), stream_ptr(x.device))
-    check(status, 'lb_linear')
+    fmt_id = LB_FMT[fmt]
+    dev = x.device
+    y = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws = Workspace.for_stream(_linear_ws_bytes(fmt_id, group, m, n, k, rank), dev.index, stream)
+    status = L.lb_linear_path(PATH[path], fmt_id, group, m, n, k, x.data_ptr(), codes.data_ptr(), _addr(scales),
+                              _addr(down), _addr(up), rank, _addr(bias), y.data_ptr(), ws.data_ptr(), ws.numel(),
+                              stream)
+    if status != OK:
+        check(status, 'lb_linear')
     return y
 
 
