@@ -129,8 +129,13 @@ int select_path(int fmt, int group, int m, int n, int k, int rank) {
 // z holds rank rounded up to 32 columns per activation row (32 for every lb_linear call).
 size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * ((rank + 31) / 32 * 32) * 2) : 0; }
 
-// z projection for the TC path at larger M runs on the tensor cores too
-bool z_on_tc(int m, int k, int rank) { return m > 32 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0); }
+// The z projection runs on lowrank_project kernels (mma.sync tiles above M = 64, where a
+// rank-32 "weight" tile would leave three quarters of a tcgen05 tile empty); LOWBIT_Z_TC=1
+// selects the tcgen05 path instead (comparison).
+bool z_on_tc(int m, int k, int rank) {
+  static const bool tc = getenv("LOWBIT_Z_TC") && getenv("LOWBIT_Z_TC")[0] == '1';
+  return tc && m > 32 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0);
+}
 
 size_t linear_ws(int path, int fmt, int group, int m, int n, int k, int rank) {
   size_t b = kHeader + z_bytes(m, rank);

@@ -18,6 +18,8 @@
 // No TMA multicast is used anywhere.  Every mbarrier wait is bounded: on timeout the
 // kernel records LB_ERR_TIMEOUT in the workspace flag, drains and returns.
 #include <cuda.h>
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace lowbit {
@@ -432,6 +434,10 @@ bool tc_supported(int fmt, int group, int m, int n, int k, int rank) {
 }
 
 int tc_block_m(int m) {
+  if (const char *env = getenv("LOWBIT_TC_BM")) {   // tuning: force the activation tile width
+    const int bm = atoi(env);
+    if (bm == 16 || bm == 32 || bm == 64 || bm == 128 || bm == 256) return bm;
+  }
   if (m <= 16) return 16;
   if (m <= 32) return 32;
   if (m <= 64) return 64;
