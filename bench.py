@@ -198,6 +198,42 @@ def dominant_kernel_roofline(device, stream, peak_gbs):
             'traffic': TRAFFIC_PER_LAUNCH.get(DOMINANT)}
 
 
+PREFILL = ('nf4', 64, 8192, 2048, 8192)   # the 1.7B gate/up shape at a prefill batch of 8192 tokens
+
+
+def prefill_roofline(device, stream, peak_tf):
+    """The prefill GEMM on the tensor cores: NF4 g64 8192x2048 with the rank-32 correction
+    at M=8192 (tcgen05 path, z projection included), back to back in one graph over two
+    weight replicas; achieved = FLOPs per call / duration vs the measured bf16 peak."""
+    import lowbit_runtime as rt
+    fmt, g, n, k, m = PREFILL
+    gen = torch.Generator(device='cpu').manual_seed(2)
+    reps = [rt.quantize_pack((torch.randn(n, k, generator=gen) * 0.02).half().to(device), fmt, g) for _ in range(2)]
+    x = torch.randn(m, k, generator=gen).half().to(device)
+    v = (torch.randn(RANK, k, generator=gen) * 1e-3).half().to(device)
+    u = (torch.randn(n, RANK, generator=gen) * 1e-3).half().to(device)
+    y = torch.empty(m, n, dtype=torch.float16, device=device)
+    launches = 8
+    with torch.cuda.stream(stream):
+        for c, sc in reps:
+            rt.linear(x, fmt, g, n, c, sc, down=v, up=u, out=y)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(launches):
+                c, sc = reps[i % 2]
+                rt.linear(x, fmt, g, n, c, sc, down=v, up=u, out=y)
+        for _ in range(2):
+            graph.replay()
+        stream.synchronize()
+        t = timed(lambda i: graph.replay(), 3, stream) / (3 * launches)
+    flops = 2 * m * n * k + 2 * m * RANK * (n + k)
+    achieved = flops / t / 1e12
+    return {'kernel': 'tc_linear_kernel<NF4, 256> (+ z projection), 8192x2048, group 64, M=8192, rank 32',
+            'bound': 'tensor', 'achieved': round(achieved, 1), 'peak': peak_tf, 'unit': 'TFLOP/s',
+            'frac': round(achieved / peak_tf, 4), 'launch_us': round(t * 1e6, 2), 'flops_per_call': flops,
+            'tensor_pipe_active': 'profiles/tc_linear_nf4_g64_m2048_8192x2048.md'}
+
+
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel (mean of
 # the two captured launches), from the committed ncu capture
 # (profiles/gemv_nf4_g64_8192x2048_m1.md).
@@ -523,6 +559,8 @@ def main():
     e2e['value'] = round(world / e2e_v, 1) if world > 1 else e2e['value']
     roof = dominant_kernel_roofline(device, stream, peak_gbs)
     roof['peak_kind'] = f'{peak_kind} HBM copy bandwidth (burst)'
+    pre_roof = prefill_roofline(device, stream, peak_tf)
+    pre_roof['peak_kind'] = f'{peak_kind} bf16 dense GEMM (burst)'
     del graphs, cells
     torch.cuda.empty_cache()
     decode = None
@@ -546,7 +584,7 @@ def main():
             'vs_baseline': None, 'dtype': 'u8 codes, fp16 io, fp32 accumulate', 'data': 'synthetic (seeded, BASELINE shapes)',
             'config': config_block(world),
             'frac_of_hbm_peak': round(value / world / peak_gbs, 4),
-            'e2e': e2e, 'roofline': roof, 'clocks': clocks.summary(),
+            'e2e': e2e, 'roofline': roof, 'prefill_roofline': pre_roof, 'clocks': clocks.summary(),
             'gpu_launches': launches_per_step_count * args.steps}
     if decode is not None:
         line['decode'] = decode

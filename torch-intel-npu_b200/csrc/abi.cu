@@ -129,11 +129,13 @@ int select_path(int fmt, int group, int m, int n, int k, int rank) {
 // z holds rank rounded up to 32 columns per activation row (32 for every lb_linear call).
 size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * ((rank + 31) / 32 * 32) * 2) : 0; }
 
-// The z projection runs on lowrank_project kernels (mma.sync tiles above M = 64, where a
-// rank-32 "weight" tile would leave three quarters of a tcgen05 tile empty); LOWBIT_Z_TC=1
-// selects the tcgen05 path instead (comparison).
+// The z projection of a tcgen05 call: mma.sync tiles up to 16384 activation rows (a rank-32
+// "weight" tile leaves three quarters of a tcgen05 tile empty, and the launch is short),
+// the tcgen05 kernel above (measured on B200: 2048 and 8192 rows faster on mma.sync,
+// 65536 rows faster on tcgen05).  LOWBIT_Z_TC=0 / 1 forces either (comparison).
 bool z_on_tc(int m, int k, int rank) {
-  static const bool tc = getenv("LOWBIT_Z_TC") && getenv("LOWBIT_Z_TC")[0] == '1';
+  static const char *env = getenv("LOWBIT_Z_TC");
+  const bool tc = env ? env[0] == '1' : m > 16384;
   return tc && m > 32 && tc_supported(LB_FMT_FP16, k, m, rank, k, 0);
 }
 
