@@ -1,6 +1,7 @@
 // The C ABI of liblowbit.so (declared in include/lowbit.h): host-side validation that
 // mirrors the reference's ValueError checks, path selection, workspace carving, status
 // codes and host-side fault injection.  No entry point allocates device memory.
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -24,6 +25,11 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
                         const uint16_t *bias, const uint16_t *resid, uint16_t *y, void *scratch, int *counters,
                         cudaStream_t st);
 size_t gemv_workspace_bytes(int fmt, int m, int n, int k);
+cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                                const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
+                                const uint16_t *bias, uint16_t *y, void *scratch, int *counters, float *zpart,
+                                int *err, cudaStream_t st, bool *fused);
+size_t gemv_fused_zpart_bytes(int m);
 cudaError_t launch_linear_generic(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
                                   const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank,
                                   const uint16_t *bias, uint16_t *y, cudaStream_t st);
@@ -126,8 +132,11 @@ int select_path(int fmt, int group, int m, int n, int k, int rank) {
   return LB_PATH_GENERIC;
 }
 
-// z holds rank rounded up to 32 columns per activation row (32 for every lb_linear call).
-size_t z_bytes(int m, int rank) { return rank > 0 ? align256(size_t(m) * ((rank + 31) / 32 * 32) * 2) : 0; }
+// z holds rank rounded up to 32 columns per activation row (32 for every lb_linear call),
+// or the fp32 K-slice partials of a projection fused into the decode GEMV.
+size_t z_bytes(int m, int rank) {
+  return rank > 0 ? align256(std::max(size_t(m) * ((rank + 31) / 32 * 32) * 2, gemv_fused_zpart_bytes(m))) : 0;
+}
 
 // The z projection of a tcgen05 call: mma.sync tiles up to 16384 activation rows (a rank-32
 // "weight" tile leaves three quarters of a tcgen05 tile empty, and the launch is short),
@@ -279,6 +288,13 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
   uint16_t *z = rank > 0 ? reinterpret_cast<uint16_t *>(ws + kHeader) : nullptr;
   uint8_t *rest = ws + kHeader + z_bytes(m, rank);
   cudaError_t e = cudaSuccess;
+  if (z && path == LB_PATH_GEMV) {   // the projection inside the GEMV launch when it qualifies
+    bool fused = false;
+    e = launch_gemv_fused_z(fmt, group, m, n, k, x, codes, scales, down, up, rank, bias, y, rest,
+                            reinterpret_cast<int *>(ws + kCounterOffset), reinterpret_cast<float *>(z), err, st, &fused);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (fused) return LB_OK;
+  }
   if (z) {
     if (path == LB_PATH_TC && z_on_tc(m, k, rank)) {
       float *zpart = reinterpret_cast<float *>(rest + align256(tc_partial_bytes(m, n, k)));

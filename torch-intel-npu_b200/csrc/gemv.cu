@@ -19,6 +19,12 @@
 // the last CTA of a row set (atomic counter, self-resetting) sums them in a fixed
 // order, so results are deterministic.  Epilogue (torch_npu_smollm.py:150-164):
 // y = half(acc) (per-row INT8 scale first), half(y + bias), half(y + half(z . U[n]^T)).
+// For large weights at up to 16 activation rows the rank-32 projection z = half(x . V^T)
+// is computed by the same launch (launch_gemv_fused_z): the first CTAs of the grid each
+// reduce one K slice of x . V^T into fp32 partials and count their arrival; the CTAs that
+// run an epilogue wait (bounded) for all slices and sum them in slice order.  The GEMV
+// of a large weight outlasts that chain, so the projection costs no launch of its own.
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 
@@ -30,6 +36,8 @@ constexpr int kWarps = 8;
 constexpr int kMaxRowGroups = 2;          // 16-row groups per warp
 constexpr int kLutWords = 256 * 64;       // NF4 table with a 256-byte entry stride
 constexpr int kMaxGemvCounters = 4096;    // arrival counters available in the workspace
+constexpr int kZArrive = kMaxGemvCounters - 2;   // fused z: slices done, epilogues done
+constexpr int kMaxZSlices = 32;
 
 struct GemvParams {
   int m, n, k, group;
@@ -51,7 +59,71 @@ struct GemvParams {
   int *counters;         // [gridDim.x] arrival counters (zero between calls)
   int prefetch;
   int gshift;            // log2(group / chunk elements) when that is a power of two, else -1
+  // fused projection (zv non-null): V [rank, k]; CTAs with blockIdx.x < zx compute K slice
+  // blockIdx.y * zx + blockIdx.x of zx * gridDim.y into zpart [slices][m][32] fp32;
+  // counters[kZArrive] counts finished slices, counters[kZArrive + 1] finished epilogues
+  // (the last resets both); err receives LB_ERR_TIMEOUT if the wait for z gives up
+  const __half *zv;
+  int zx;
+  float *zpart;
+  int *err;
 };
+
+__device__ __forceinline__ int ld_acquire(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One K slice of z^T = V x^T for up to 8 * NCOL activation rows: warp w owns ranks
+// 4w .. 4w + 3, lane l the slice's 16-byte chunks l, l + 32, ...; fp16 products are exact
+// and summed in fp32 (lane order, then a butterfly), one partial per (row, rank).
+template <int NCOL>
+__device__ __forceinline__ void gemv_z_slice(const GemvParams &p) {
+  constexpr int MR = 8 * NCOL;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int slices = p.zx * gridDim.y, slice = blockIdx.y * p.zx + blockIdx.x;
+  const int chunks = p.k / 8;
+  const int c0 = int(int64_t(slice) * chunks / slices), c1 = int(int64_t(slice + 1) * chunks / slices);
+  float acc[4][MR];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[r][m] = 0.f;
+  for (int c = c0 + lane; c < c1; c += 32) {
+    uint4 v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int rr = 4 * warp + r;
+      v[r] = rr < p.rank ? *reinterpret_cast<const uint4 *>(p.zv + int64_t(rr) * p.k + 8 * c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (m >= p.m) break;
+      const uint4 xv = *reinterpret_cast<const uint4 *>(p.x + int64_t(m) * p.k + 8 * c);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        fma2_f16_f32(acc[r][m], v[r].x, xv.x);
+        fma2_f16_f32(acc[r][m], v[r].y, xv.y);
+        fma2_f16_f32(acc[r][m], v[r].z, xv.z);
+        fma2_f16_f32(acc[r][m], v[r].w, xv.w);
+      }
+    }
+  }
+  float *out = p.zpart + int64_t(slice) * p.m * 32;
+#pragma unroll
+  for (int m = 0; m < MR; ++m) {
+    if (m >= p.m) break;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float sum = warp_sum(acc[r][m]);
+      if (lane == 0) out[m * 32 + 4 * warp + r] = sum;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(p.counters + kZArrive, 1);
+}
 
 // NCOL = 8-column groups of activation rows (M <= 8 NCOL).  Up to 16 columns the x pairs
 // of a round are loaded up front and each warp may hold two row groups with two
@@ -75,12 +147,21 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   uint32_t *lut = smem + red_words<NCOL>();
   __shared__ int s_last;
 
+  if constexpr (NCOL <= 2) {
+    if (p.zv && int(blockIdx.x) < p.zx) {
+      pdl_launch();
+      pdl_wait();
+      gemv_z_slice<NCOL>(p);
+      return;
+    }
+  }
+  const int bx = int(blockIdx.x) - (p.zv ? p.zx : 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int wr = kWarps / p.warps_k;
   const int kw = warp % p.warps_k, rw = warp / p.warps_k;
   const int rows_cta = 16 * wr * p.rpw;
-  const int row0 = blockIdx.x * rows_cta;
+  const int row0 = bx * rows_cta;
   const int wrow0 = row0 + 16 * p.rpw * rw;   // this warp's first row
   const int64_t row_bytes = int64_t(p.k) * FmtTraits<FMT>::BITS / 8;
   const int chunks = p.k / E;
@@ -262,7 +343,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(p.counters + blockIdx.x, 1) == splits - 1;
+    if (threadIdx.x == 0) s_last = atomicAdd(p.counters + bx, 1) == splits - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
@@ -273,7 +354,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       for (int sp = 0; sp < splits; ++sp) v += __ldcg(p.partial + sp * mn + int64_t(mm) * p.n + n);
       red[rl * LDC + mm] = v;   // warp-0 slot reused for the total
     }
-    if (threadIdx.x == 0) p.counters[blockIdx.x] = 0;   // ready for the next call
+    if (threadIdx.x == 0) p.counters[bx] = 0;   // ready for the next call
     __syncthreads();
   }
 
@@ -288,7 +369,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     __syncthreads();
   }
 
-  if (!p.z) {
+  if (!p.z && !p.zv) {
     for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
       const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
       if (n >= p.n) continue;
@@ -307,7 +388,39 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   // operand, zs / 16 m16n8k16 tiles per 8-column group; then
   // y = half(half(half(acc) + bias) + delta) as torch_npu_smollm.py:150-164 stages it, and
   // half(y + residual) when a residual is fused (torch_npu_smollm.py:192).
-  const int ktiles = p.zs / 16;
+  const __half *zsrc = p.z;
+  int zstride = p.zs;
+  if constexpr (NCOL <= 2) {
+    __shared__ __align__(16) __half s_z[16 * 32];
+    if (p.zv) {
+      // wait (bounded) for every K slice of z, then z = half(sum of the slices in order)
+      if (threadIdx.x == 0) {
+        const int slices = p.zx * gridDim.y;
+        if (ld_acquire(p.counters + kZArrive) < slices) {
+          const long long t0 = clock64();
+          while (ld_acquire(p.counters + kZArrive) < slices)
+            if (clock64() - t0 > kWaitCycles) { atomicExch(p.err, LB_ERR_TIMEOUT); break; }
+        }
+      }
+      __syncthreads();
+      const int slices = p.zx * gridDim.y;
+      for (int i = threadIdx.x; i < p.m * 32; i += blockDim.x) {
+        float sum = 0.f;
+        if ((i & 31) < p.rank)
+          for (int sl = 0; sl < slices; ++sl) sum += __ldcg(p.zpart + int64_t(sl) * p.m * 32 + i);
+        s_z[i] = __float2half_rn(sum);
+      }
+      __syncthreads();
+      // the last epilogue leaves both counters at zero for the next call
+      if (threadIdx.x == 0 && atomicAdd(p.counters + kZArrive + 1, 1) == int(gridDim.x) - p.zx - 1) {
+        p.counters[kZArrive] = 0;
+        p.counters[kZArrive + 1] = 0;
+      }
+      zsrc = s_z;
+      zstride = 32;
+    }
+  }
+  const int ktiles = zstride / 16;
   for (int rg = warp; rg < rows_cta / 16; rg += kWarps) {
     const int rl0 = rg * 16;
 #pragma unroll
@@ -331,7 +444,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         }
         uint32_t b0 = 0, b1 = 0;
         if (mz < p.m) {
-          const uint32_t *zr = reinterpret_cast<const uint32_t *>(p.z + int64_t(mz) * p.zs);
+          const uint32_t *zr = reinterpret_cast<const uint32_t *>(zsrc + int64_t(mz) * zstride);
           b0 = zr[8 * kt + t];
           b1 = zr[8 * kt + t + 4];
         }
@@ -585,7 +698,7 @@ static GemvPlan gemv_plan_search(int fmt, int m, int n, int k) {
     for (int rpw = 1; rpw <= (m > 16 ? 1 : kMaxRowGroups); rpw *= 2) {
       for (int sp = 1; sp <= 16; sp *= 2) {
         if (fwk && (wk != fwk || rpw != frpw || sp != fsp)) continue;
-        if (sp > 1 && ((groups + (kWarps / wk) * rpw - 1) / ((kWarps / wk) * rpw)) > kMaxGemvCounters) continue;
+        if (sp > 1 && ((groups + (kWarps / wk) * rpw - 1) / ((kWarps / wk) * rpw)) > kZArrive) continue;
         const int kbs = (kblocks + sp - 1) / sp;
         if (sp > 1 && kbs < wk) break;
         if (wk > 1 && kbs < wk) continue;
@@ -613,6 +726,45 @@ size_t gemv_workspace_bytes(int fmt, int m, int n, int k) {
   const GemvPlan pl = gemv_plan(fmt, m, n, k);
   if (pl.splits <= 1) return 0;
   return size_t(pl.splits) * m * n * sizeof(float);
+}
+
+// CTAs of one kernel that fit on the device at once (cached per kernel and device).
+static int resident_ctas(const void *kern, size_t smem) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const uint64_t key = (uint64_t(reinterpret_cast<uintptr_t>(kern)) << 6) ^ uint64_t(dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int per_sm = 0, sms = 0;
+  if (ensure_dyn_smem(kern, int(smem)) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * kWarps, smem) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = per_sm * sms;
+  return per_sm * sms;
+}
+template <int FMT, int NCOL> static size_t gemv_smem_v() {
+  return size_t(red_words<NCOL>()) * sizeof(float) + (FMT == LB_FMT_NF4 ? size_t(kLutWords) * 4 : 0);
+}
+template <int FMT> static int resident_ctas_f(int ncol) {
+  return ncol == 1 ? resident_ctas(reinterpret_cast<const void *>(gemv_kernel<FMT, 1>), gemv_smem_v<FMT, 1>())
+                   : resident_ctas(reinterpret_cast<const void *>(gemv_kernel<FMT, 2>), gemv_smem_v<FMT, 2>());
+}
+
+// Activation rows and weight bytes from which the projection is fused into the GEMV
+// launch (measured on B200: from ~4 MB of codes the GEMV outlasts the slice chain; below
+// it the separate projection launch, which overlaps the GEMV's weight preload, is faster).
+constexpr int kFuseZMaxRows = 16;
+constexpr int64_t kFuseZMinBytes = int64_t(4) << 20;
+
+size_t gemv_fused_zpart_bytes(int m) {
+  return m <= kFuseZMaxRows ? size_t(kMaxZSlices) * m * 32 * sizeof(float) : 0;
 }
 
 template <int FMT, int NCOL>
@@ -692,6 +844,70 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   size_t smem = size_t(kWarps) * 64 * 16 * sizeof(float);
   if (fmt == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
   const dim3 grid(pl.ctas_x, pl.splits);
+  switch (fmt) {
+    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st);
+    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st);
+    case LB_FMT_INT8: return launch_gemv_f<LB_FMT_INT8>(p, ncol, grid, smem, st);
+    default: return launch_gemv_f<LB_FMT_FP16>(p, ncol, grid, smem, st);
+  }
+}
+
+// The decode GEMV with its rank <= 32 correction projection in the same launch, when the
+// problem qualifies (<= kFuseZMaxRows rows, >= kFuseZMinBytes of codes, the whole grid
+// resident at once so that the epilogues' wait for the slices always ends); *fused says
+// whether it launched.  zpart: gemv_fused_zpart_bytes(m) of workspace; counters as for
+// launch_gemv (two more at kZArrive); err: the workspace status word.
+cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                                const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
+                                const uint16_t *bias, uint16_t *y, void *scratch, int *counters, float *zpart,
+                                int *err, cudaStream_t st, bool *fused) {
+  *fused = false;
+  const int bits = fmt == LB_FMT_INT8 ? 8 : (fmt == LB_FMT_FP16 ? 16 : 4);
+  if (m > kFuseZMaxRows || rank < 1 || rank > 32 || !down || !zpart || !err ||
+      int64_t(n) * k * bits / 8 < kFuseZMinBytes)
+    return cudaSuccess;
+  const GemvPlan pl = gemv_plan(fmt, m, n, k);
+  const int ncol = m <= 8 ? 1 : 2;
+  const int want = std::min(kMaxZSlices, std::max(1, (k / 8 + 31) / 32));
+  const int zx = std::max(1, want / pl.splits);
+  int cap = 0;
+  switch (fmt) {
+    case LB_FMT_INT4: cap = resident_ctas_f<LB_FMT_INT4>(ncol); break;
+    case LB_FMT_NF4: cap = resident_ctas_f<LB_FMT_NF4>(ncol); break;
+    case LB_FMT_INT8: cap = resident_ctas_f<LB_FMT_INT8>(ncol); break;
+    default: cap = resident_ctas_f<LB_FMT_FP16>(ncol); break;
+  }
+  if (int64_t(zx + pl.ctas_x) * pl.splits > cap) return cudaSuccess;
+  GemvParams p = {};
+  p.m = m; p.n = n; p.k = k; p.group = fmt == LB_FMT_FP16 ? k : group;
+  p.x = reinterpret_cast<const __half *>(x);
+  p.codes = codes;
+  p.scales = reinterpret_cast<const __half *>(scales);
+  p.zv = reinterpret_cast<const __half *>(down);
+  p.zx = zx;
+  p.zpart = zpart;
+  p.err = err;
+  p.up = reinterpret_cast<const __half *>(up);
+  p.rank = rank;
+  p.zs = 32;
+  p.bias = reinterpret_cast<const __half *>(bias);
+  p.y = reinterpret_cast<__half *>(y);
+  p.warps_k = pl.warps_k;
+  p.rpw = pl.rpw;
+  p.kblocks = (k / gemv_elems(fmt) + 3) / 4;
+  p.kb_per_split = pl.kb_per_split;
+  if (pl.splits > 1) p.partial = static_cast<float *>(scratch);
+  p.counters = counters;
+  p.prefetch = gemv_prefetch_mode();
+  p.gshift = -1;
+  {
+    const int cpg = p.group / gemv_elems(fmt);
+    if (fmt != LB_FMT_FP16 && p.group % gemv_elems(fmt) == 0 && cpg > 0 && (cpg & (cpg - 1)) == 0)
+      for (p.gshift = 0; (1 << p.gshift) < cpg; ++p.gshift) {}
+  }
+  *fused = true;
+  const dim3 grid(pl.ctas_x + zx, pl.splits);
+  size_t smem = 0;
   switch (fmt) {
     case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st);
     case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st);

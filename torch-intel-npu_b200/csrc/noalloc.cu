@@ -25,14 +25,22 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
                         const uint16_t *scales, const uint16_t *z, int zs, const uint16_t *up, int rank,
                         const uint16_t *bias, const uint16_t *resid, uint16_t *y, void *scratch, int *counters,
                         cudaStream_t st);
+cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
+                                const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
+                                const uint16_t *bias, uint16_t *y, void *scratch, int *counters, float *zpart,
+                                int *err, cudaStream_t st, bool *fused);
+size_t gemv_fused_zpart_bytes(int m);
 }  // namespace lowbit_host
 
 namespace {
 
-// Layout: [0, 16 KiB) arrival counters (4096 ints) | [16 KiB, 20 KiB) z | rest: partials.
+// Layout: [0, 16 KiB) arrival counters (4096 ints) | [16 KiB, +256) status word (a fused
+// projection's timed-out wait) | then 64 KiB of z (or the fused projection's fp32 slices) |
+// rest: partials.
 constexpr size_t kCounterBytes = 4096 * sizeof(int);
-constexpr size_t kZOffset = kCounterBytes;
-constexpr size_t kZBytes = 4096;
+constexpr size_t kStatusOffset = kCounterBytes;
+constexpr size_t kZOffset = kStatusOffset + 256;
+constexpr size_t kZBytes = 64 << 10;
 constexpr size_t kPartialOffset = kZOffset + kZBytes;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[LB_NOALLOC_SCRATCH_BYTES];
@@ -76,7 +84,7 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
   if (!gemv_supported(fmt, group, m, n, k) || !aligned16(x) || !aligned16(codes) || !aligned16(y) ||
       (down && (!aligned16(down) || !aligned16(up))))
     return LB_ERR_UNSUPPORTED;   // only the decode GEMV (M <= 64, aligned rows) has this variant
-  if (size_t(m) * 32 * 2 > kZBytes ||
+  if (size_t(m) * 32 * 2 > kZBytes || gemv_fused_zpart_bytes(m) > kZBytes ||
       gemv_workspace_bytes(fmt, m, n, k) > size_t(LB_NOALLOC_SCRATCH_BYTES) - kPartialOffset)
     return LB_ERR_WORKSPACE;     // the problem needs more scratch than the fixed array holds
   void *base = nullptr;
@@ -87,6 +95,13 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
   int *counters = reinterpret_cast<int *>(s);
   // The array keeps whatever the previous call left; the counters must start at zero.
   e = cudaMemsetAsync(counters, 0, kCounterBytes, st);
+  if (e == cudaSuccess && rank > 0) {   // the same fused projection lb_linear would run
+    bool fused = false;
+    e = launch_gemv_fused_z(fmt, group, m, n, k, x, codes, scales, down, up, rank, bias, y, s + kPartialOffset,
+                            counters, reinterpret_cast<float *>(s + kZOffset),
+                            reinterpret_cast<int *>(s + kStatusOffset), st, &fused);
+    if (e != cudaSuccess || fused) return e == cudaSuccess ? LB_OK : LB_ERR_CUDA;
+  }
   uint16_t *z = nullptr;
   if (e == cudaSuccess && rank > 0) {
     z = reinterpret_cast<uint16_t *>(s + kZOffset);
