@@ -52,7 +52,10 @@ struct GemvParams {
   const __half *bias;    // [n] or null
   __half *y;             // [m, n]
   int warps_k;           // warps splitting a CTA's K range (1, 2, 4, 8)
+  int wk_shift;          // log2(warps_k)
   int rpw;               // 16-row groups per warp (<= kMaxRowGroups)
+  int rows_shift;        // log2(rows per CTA) = log2(16 * (8 / warps_k) * rpw)
+  int gpr;               // scale groups per row (1 for FP16)
   int kblocks;           // 64-byte K blocks per row
   int kb_per_split;      // K blocks per CTA (gridDim.y splits)
   float *partial;        // [splits, m, n] fp32 when gridDim.y > 1
@@ -158,9 +161,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   const int bx = int(blockIdx.x) - (p.zv ? p.zx : 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int wr = kWarps / p.warps_k;
-  const int kw = warp % p.warps_k, rw = warp / p.warps_k;
-  const int rows_cta = 16 * wr * p.rpw;
+  const int kw = warp & (p.warps_k - 1), rw = warp >> p.wk_shift;
+  const int rows_cta = 1 << p.rows_shift;
   const int row0 = bx * rows_cta;
   const int wrow0 = row0 + 16 * p.rpw * rw;   // this warp's first row
   const int64_t row_bytes = int64_t(p.k) * FmtTraits<FMT>::BITS / 8;
@@ -168,7 +170,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   const int kb0 = blockIdx.y * p.kb_per_split;
   const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
 
-  const int groups_per_row = FMT == LB_FMT_FP16 ? 1 : p.k / p.group;
+  const int groups_per_row = p.gpr;
   const bool per_row_scale = FMT == LB_FMT_INT8 && p.group == p.k;
   // One round of weight loads: two K blocks x rpw row groups x rows g / g+8, with scales.
   // Per-lane bases of row g (row g+8 and the next row group are fixed offsets from it).
@@ -332,14 +334,23 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
 
   const int splits = gridDim.y;
   const int outs = rows_cta * p.m;
+  // sum of the K-split warps' partials of entry (rl, mm), all loads issued first
+  auto warp_total = [&](int rl, int mm) {
+    float v[kWarps];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v[w] = w < p.warps_k ? red[(w * rows_cta + rl) * LDC + mm] : 0.f;
+    float sum = v[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w)
+      if (w < p.warps_k) sum += v[w];
+    return sum;
+  };
   if (splits > 1) {
     const int64_t mn = int64_t(p.m) * p.n;
     for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
-      const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+      const int mm = idx >> p.rows_shift, rl = idx & (rows_cta - 1), n = row0 + rl;
       if (n >= p.n) continue;
-      float v = 0.f;
-      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * LDC + mm];
-      p.partial[blockIdx.y * mn + int64_t(mm) * p.n + n] = v;
+      p.partial[blockIdx.y * mn + int64_t(mm) * p.n + n] = warp_total(rl, mm);
     }
     __threadfence();
     __syncthreads();
@@ -348,7 +359,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     if (!s_last) return;
     __threadfence();
     for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
-      const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+      const int mm = idx >> p.rows_shift, rl = idx & (rows_cta - 1), n = row0 + rl;
       if (n >= p.n) continue;
       float v = 0.f;
       for (int sp = 0; sp < splits; ++sp) v += __ldcg(p.partial + sp * mn + int64_t(mm) * p.n + n);
@@ -358,22 +369,13 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     __syncthreads();
   }
 
-  // Totals into the warp-0 slot (each thread owns its (row, column) entries).
-  if (splits == 1 && p.warps_k > 1) {
-    for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
-      const int mm = idx / rows_cta, rl = idx % rows_cta;
-      float v = 0.f;
-      for (int w = 0; w < p.warps_k; ++w) v += red[(w * rows_cta + rl) * LDC + mm];
-      red[rl * LDC + mm] = v;
-    }
-    __syncthreads();
-  }
-
   if (!p.z && !p.zv) {
+    // one pass: total (over the K-split warps unless the cross-CTA sum is in slot 0), scale,
+    // bias, residual, store
     for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
-      const int mm = idx / rows_cta, rl = idx % rows_cta, n = row0 + rl;
+      const int mm = idx >> p.rows_shift, rl = idx & (rows_cta - 1), n = row0 + rl;
       if (n >= p.n) continue;
-      float v = red[rl * LDC + mm];
+      float v = splits > 1 ? red[rl * LDC + mm] : warp_total(rl, mm);
       if (per_row_scale) v *= __half2float(p.scales[n]);
       __half yq = __float2half_rn(v);
       if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
@@ -381,6 +383,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       p.y[int64_t(mm) * p.n + n] = yq;
     }
     return;
+  }
+
+  // Totals into the warp-0 slot (each thread owns its (row, column) entries).
+  if (splits == 1 && p.warps_k > 1) {
+    for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+      const int mm = idx >> p.rows_shift, rl = idx & (rows_cta - 1);
+      red[rl * LDC + mm] = warp_total(rl, mm);   // only this thread reads or writes entry (rl, mm)
+    }
+    __syncthreads();
   }
 
   // Correction delta = half(z . U[n]^T) on the tensor cores: per 16-row group, U rows
@@ -685,6 +696,19 @@ static GemvPlan gemv_plan(int fmt, int m, int n, int k) {
   return pl;
 }
 
+static int ilog2(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return s;
+}
+
+// Per-launch constants the kernel would otherwise derive with integer divisions.
+static void set_shape_fields(GemvParams &p, int fmt, const GemvPlan &pl) {
+  p.wk_shift = ilog2(pl.warps_k);
+  p.rows_shift = ilog2(16 * (kWarps / pl.warps_k) * pl.rpw);
+  p.gpr = fmt == LB_FMT_FP16 ? 1 : p.k / p.group;
+}
+
 static GemvPlan gemv_plan_search(int fmt, int m, int n, int k) {
   const int e = gemv_elems(fmt);
   const int kblocks = (k / e + 3) / 4;
@@ -827,6 +851,7 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   const GemvPlan pl = gemv_plan(fmt, m, n, k);
   p.warps_k = pl.warps_k;
   p.rpw = pl.rpw;
+  set_shape_fields(p, fmt, pl);
   p.kblocks = (k / gemv_elems(fmt) + 3) / 4;
   p.kb_per_split = pl.kb_per_split;
   if (pl.splits > 1) {
@@ -894,6 +919,7 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
   p.y = reinterpret_cast<__half *>(y);
   p.warps_k = pl.warps_k;
   p.rpw = pl.rpw;
+  set_shape_fields(p, fmt, pl);
   p.kblocks = (k / gemv_elems(fmt) + 3) / 4;
   p.kb_per_split = pl.kb_per_split;
   if (pl.splits > 1) p.partial = static_cast<float *>(scratch);
