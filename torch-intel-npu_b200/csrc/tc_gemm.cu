@@ -3,14 +3,18 @@
 // Orientation ("weights as A"): one CTA owns 128 weight rows (the MMA M dimension) and
 // BM activation rows (the MMA N dimension, 16..256).  Per 64-wide K stage:
 //   * warp 0 (one lane) TMA-loads the packed code tile [128 rows x 32|64 bytes] and the
-//     activation tile [BM x 64] fp16 (128-byte swizzle) -- fp16 weights are TMA-loaded
-//     straight into the A buffer;
-//   * warps 2..5 (128 threads, one weight row each) dequantize the codes exactly as the
-//     reference does (rn16(code * scale)) into the K-major 128B-swizzled A buffer;
+//     activation tile [BM x 64] fp16 (128-byte swizzle) into one of S stage buffers --
+//     fp16 weights are TMA-loaded straight into the stage's A buffer;
+//   * warps 2..9 dequantize the codes exactly as the reference does (rn16(code * scale))
+//     into one of two K-major 128B-swizzled A buffers (the A ring is decoupled from the
+//     TMA ring: an A buffer is busy only from dequant to MMA completion, a TMA stage from
+//     the copy's issue on, so two A buffers free the room for a fourth TMA stage);
 //   * warp 1 (one lane) issues 4 x tcgen05.mma (M=128, N=BM, K=16, fp16 in, fp32 TMEM
-//     accumulate) and commits to the stage's "empty" barrier.
+//     accumulate) and commits to the stage's and the A buffer's "empty" barriers.
 // The rank-32 correction is a second TMEM accumulator: U tile [128 x 32] and z tile
-// [BM x 32] (64-byte swizzle) feed two more MMAs, so delta = z.U^T lands beside y_q.
+// [BM x 32] (64-byte swizzle) feed two more MMAs, issued before the main loop (for the
+// dequant formats the two tiles are loaded into the two A buffers, which the dequant
+// warps take over once those MMAs complete), so delta = z.U^T lands beside y_q.
 // Epilogue (warps 2..5): tcgen05.ld, per-row INT8 scale, y = half(half(acc)+bias),
 // y = half(y + half(delta)), stored transposed to y[m, n].
 // Split-K (small M): each split writes fp32 partials to the caller's workspace and
@@ -75,10 +79,12 @@ template <> struct TcFmt<LB_FMT_NF4> { static constexpr int CODE_BYTES = 32; };
 template <> struct TcFmt<LB_FMT_INT8> { static constexpr int CODE_BYTES = 64; };
 template <> struct TcFmt<LB_FMT_FP16> { static constexpr int CODE_BYTES = 0; };
 
-template <int BM> struct TcStages { static constexpr int S = BM >= 256 ? 3 : (BM >= 128 ? 4 : 6); };
+template <int BM> struct TcStages { static constexpr int S = BM >= 256 ? 4 : 6; };
 
 template <int FMT, int BM> struct TcLayout {
-  static constexpr int S = TcStages<BM>::S;
+  static constexpr bool kDeq = FMT != LB_FMT_FP16;
+  static constexpr int S = TcStages<BM>::S;          // TMA stages
+  static constexpr int SA = kDeq ? (BM >= 256 ? 3 : 2) : S;   // A buffers (fp16 weight tiles ride the TMA stages)
   static constexpr int A_BYTES = 128 * 128;          // 128 rows x 64 fp16
   static constexpr int B_BYTES = BM * 128;           // BM rows x 64 fp16
   static constexpr int C_BYTES = 128 * TcFmt<FMT>::CODE_BYTES;
@@ -86,14 +92,18 @@ template <int FMT, int BM> struct TcLayout {
   static constexpr int B2_BYTES = BM * 64;           // z tile
   static constexpr int LUT_BYTES = FMT == LB_FMT_NF4 ? 256 * 32 * 4 : 0;
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + S * A_BYTES;
-  static constexpr int OFF_A2 = OFF_B + S * B_BYTES;
-  static constexpr int OFF_B2 = OFF_A2 + A2_BYTES;
-  static constexpr int OFF_C = ((OFF_B2 + B2_BYTES + 1023) / 1024) * 1024;
+  static constexpr int OFF_B = OFF_A + SA * A_BYTES;
+  // U and z: A buffers 0 and 1 for the dequant formats, a region of their own for fp16
+  static constexpr int OFF_A2 = kDeq ? OFF_A : OFF_B + S * B_BYTES;
+  static constexpr int OFF_B2 = kDeq ? OFF_A + A_BYTES : OFF_A2 + A2_BYTES;
+  static constexpr int OFF_C = (((kDeq ? OFF_B + S * B_BYTES : OFF_B2 + B2_BYTES) + 1023) / 1024) * 1024;
   static constexpr int OFF_LUT = OFF_C + S * C_BYTES;
   static constexpr int OFF_BAR = ((OFF_LUT + LUT_BYTES + 15) / 16) * 16;
-  static constexpr int BAR_BYTES = (3 * S + 2) * 8 + 32;
+  static constexpr int NBARS = 2 * S + 2 * SA + 2;
+  static constexpr int BAR_BYTES = NBARS * 8 + 32;
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
+  static_assert(A2_BYTES <= A_BYTES && B2_BYTES <= A_BYTES, "U and z tiles fit an A buffer");
+  static_assert(TOTAL <= 232448, "shared memory per CTA");
 };
 
 struct TcParams {
@@ -115,7 +125,8 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return uint32_t((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-constexpr int kDequantWarps = 8;
+constexpr int kDequantWarps = 16;
+constexpr int kStageGroups = kDequantWarps / 8;   // dequant warp groups working on alternate stages
 constexpr int kTcThreads = 32 * (2 + kDequantWarps);
 
 template <int FMT, int BM>
@@ -128,11 +139,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
+  constexpr int SA = L::SA;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
-  // bars: full_tma[S], full_a[S], empty[S], corr_full, acc_full
-  const uint32_t bar_full_tma = smem_u32(bars), bar_full_a = smem_u32(bars + S), bar_empty = smem_u32(bars + 2 * S);
-  const uint32_t bar_corr = smem_u32(bars + 3 * S), bar_acc = smem_u32(bars + 3 * S + 1);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 2);
+  // bars: full_tma[S], empty[S] (TMA stages), full_a[SA], empty_a[SA] (A buffers), corr_full, acc_full
+  const uint32_t bar_full_tma = smem_u32(bars), bar_empty = smem_u32(bars + S);
+  const uint32_t bar_full_a = smem_u32(bars + 2 * S), bar_empty_a = smem_u32(bars + 2 * S + SA);
+  const uint32_t bar_corr = smem_u32(bars + 2 * S + 2 * SA), bar_acc = smem_u32(bars + 2 * S + 2 * SA + 1);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::NBARS);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -149,8 +162,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(bar_full_tma + 8 * s, 1);
-      mbar_init(bar_full_a + 8 * s, kDequantWarps);   // one arrive per dequant warp
       mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < SA; ++a) {
+      mbar_init(bar_full_a + 8 * a, kDequantWarps / kStageGroups);   // one arrive per warp of a group
+      mbar_init(bar_empty_a + 8 * a, 1);
     }
     mbar_init(bar_corr, 1);
     mbar_init(bar_acc, 1);
@@ -203,35 +219,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------ MMA issuer --------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(128, BM);
-      for (int i = 0; i < nst; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(bar_full_tma + 8 * s, ph, abort_flag)) break;
-        if (kDequant && !mbar_wait(bar_full_a + 8 * s, ph, abort_flag)) break;
+      bool run = true;
+      if (corr) {
+        run = mbar_wait(bar_corr, 0, abort_flag);
+        if (run) {
+          tc_fence_after();
+          const uint64_t ad = umma_desc(sbase + L::OFF_A2, 512, kSwizzle64);
+          const uint64_t bd = umma_desc(sbase + L::OFF_B2, 512, kSwizzle64);
+          umma_f16(tmem_corr, ad, bd, idesc, 0u);
+          umma_f16(tmem_corr, ad + 2, bd + 2, idesc, 1u);
+          if (kDequant) {   // U and z sit in A buffers 0 and 1: hand them to the dequant warps
+            umma_commit(bar_empty_a);
+            umma_commit(bar_empty_a + 8);
+          }
+        }
+      }
+      for (int i = 0; run && i < nst; ++i) {
+        const int s = i % S, a = i % SA;
+        if (!mbar_wait(bar_full_tma + 8 * s, (i / S) & 1, abort_flag)) break;
+        if (kDequant && !mbar_wait(bar_full_a + 8 * a, (i / SA) & 1, abort_flag)) break;
         tc_fence_after();
-        const uint64_t ad = umma_desc(sbase + L::OFF_A + s * L::A_BYTES, 1024, kSwizzle128);
+        const uint64_t ad = umma_desc(sbase + L::OFF_A + a * L::A_BYTES, 1024, kSwizzle128);
         const uint64_t bd = umma_desc(sbase + L::OFF_B + s * L::B_BYTES, 1024, kSwizzle128);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_f16(tmem_acc, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar_empty + 8 * s);
-      }
-      if (corr && !*abort_flag && mbar_wait(bar_corr, 0, abort_flag)) {
-        tc_fence_after();
-        const uint64_t ad = umma_desc(sbase + L::OFF_A2, 512, kSwizzle64);
-        const uint64_t bd = umma_desc(sbase + L::OFF_B2, 512, kSwizzle64);
-        umma_f16(tmem_corr, ad, bd, idesc, 0u);
-        umma_f16(tmem_corr, ad + 2, bd + 2, idesc, 1u);
+        if (kDequant) umma_commit(bar_empty_a + 8 * a);
       }
       umma_commit(bar_acc);  // fires when every MMA issued above has completed
     }
   } else {
     // --------------------- dequant (mainloop) + epilogue ----------------------
-    // kDequantWarps warps: thread t handles weight row (t % 128) and the (t / 128)-th
-    // 32-element half of each 64-wide stage, so every SM sub-partition runs two dequant
-    // warps and the code-to-fp16 latency of one hides behind the other.
+    // kDequantWarps warps in kStageGroups groups of 8: group g dequantizes the stages
+    // i = g, g + kStageGroups, ..., so consecutive stages are in flight at once; within a
+    // group thread t handles weight row (t % 128) and the ((t / 128) % 2)-th 32-element half
+    // of the stage, and every SM sub-partition runs two warps of each group.
+    constexpr int kParts = 2, EPP = 64 / kParts;
     const int t = threadIdx.x - 64;
-    const int drow = t & 127, part = t >> 7;
+    const int drow = t & 127, part = (t >> 7) & 1, group = t >> 8;
     if (kDequant) {
       const int n = n0 + drow;
       const bool nok = n < p.n;
@@ -243,27 +269,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __half2 ring[kScaleAhead];
       auto load_scale = [&](int i) -> __half2 {
         if (per_row || !nok || i >= nst) return __float2half2_rn(1.f);
-        const __half v = p.scales[int64_t(n) * gpr + ((st_begin + i) * 64 + part * 32) / p.group];
+        const __half v = p.scales[int64_t(n) * gpr + ((st_begin + i) * 64 + part * EPP) / p.group];
         return __halves2half2(v, v);
       };
       pdl_wait();
 #pragma unroll
-      for (int j = 0; j < kScaleAhead; ++j) ring[j] = load_scale(j);
-      for (int i = 0; i < nst; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
+      for (int j = 0; j < kScaleAhead; ++j) ring[j] = load_scale(group + kStageGroups * j);
+      // uses of A buffer a: the correction tiles (buffers 0 and 1, if any), then the main
+      // stages i = a, a + SA, ...
+      for (int i = group; i < nst; i += kStageGroups) {
+        const int s = i % S, a = i % SA;
+        const int first_use = corr && a < 2 ? 1 : 0;
         const __half2 sc = ring[0];
 #pragma unroll
         for (int j = 0; j + 1 < kScaleAhead; ++j) ring[j] = ring[j + 1];
-        ring[kScaleAhead - 1] = load_scale(i + kScaleAhead);
-        if (!mbar_wait(bar_full_tma + 8 * s, ph, abort_flag)) break;
+        ring[kScaleAhead - 1] = load_scale(i + kStageGroups * kScaleAhead);
+        if (!mbar_wait(bar_full_tma + 8 * s, (i / S) & 1, abort_flag)) break;
+        const int use = i / SA + first_use;   // the buffer's previous use must have left the tensor cores
+        if (use > 0 && !mbar_wait(bar_empty_a + 8 * a, (use - 1) & 1, abort_flag)) break;
         const uint8_t *crow = smem + L::OFF_C + s * L::C_BYTES + drow * TcFmt<FMT>::CODE_BYTES;
-        uint8_t *abuf = smem + L::OFF_A + s * L::A_BYTES;
+        uint8_t *abuf = smem + L::OFF_A + a * L::A_BYTES;
         if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
-          const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * part);
-          const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+          constexpr int W = EPP / 8;   // 32-bit code words (8 codes each) of this part
+          uint32_t wv[W];
+          if constexpr (W == 4) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * part);
+            wv[0] = c.x; wv[1] = c.y; wv[2] = c.z; wv[3] = c.w;
+          } else {
+            const uint2 c = *reinterpret_cast<const uint2 *>(crow + 8 * part);
+            wv[0] = c.x; wv[1] = c.y;
+          }
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
+          for (int w = 0; w < W; ++w) {
             uint32_t o[4];
             if constexpr (FMT == LB_FMT_INT4) {
               uint32_t q[4];
@@ -281,17 +318,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) o[j] = h2_as_u32(__hmul2(u32_as_h2(o[j]), sc));
-            *reinterpret_cast<uint4 *>(abuf + swz128(drow, part * 4 + w)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4 *>(abuf + swz128(drow, part * W + w)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
-        } else {  // INT8: this thread's 32 bytes -> 4 chunks of 8 halves
-          uint32_t wv[8];
+        } else {  // INT8: this thread's EPP bytes -> EPP / 8 chunks of 8 halves
+          constexpr int V = EPP / 16;
+          uint32_t wv[4 * V];
 #pragma unroll
-          for (int v = 0; v < 2; ++v) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 32 * part + 16 * v);
+          for (int v = 0; v < V; ++v) {
+            const uint4 c = *reinterpret_cast<const uint4 *>(crow + EPP * part + 16 * v);
             wv[4 * v] = c.x; wv[4 * v + 1] = c.y; wv[4 * v + 2] = c.z; wv[4 * v + 3] = c.w;
           }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2 * V; ++j) {
             uint32_t a[2], b[2], o[4];
             int8_word_to_h2(wv[2 * j], a);       // (e0,e2) (e1,e3)
             int8_word_to_h2(wv[2 * j + 1], b);   // (e4,e6) (e5,e7)
@@ -303,12 +341,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
               for (int q = 0; q < 4; ++q) o[q] = h2_as_u32(__hmul2(u32_as_h2(o[q]), sc));
             }
-            *reinterpret_cast<uint4 *>(abuf + swz128(drow, part * 4 + j)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4 *>(abuf + swz128(drow, part * (EPP / 8) + j)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_full_a + 8 * s);
+        if (lane == 0) mbar_arrive(bar_full_a + 8 * a);
       }
     } else {
       pdl_wait();
@@ -318,9 +356,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_acc, 0, abort_flag));
     tc_fence_after();
     const int row = 32 * (warp & 3) + lane;          // TMEM lane this warp may access
-    // two warps per TMEM lane quadrant split the BM columns; a 16-column tile stays whole
-    constexpr int kColsPerWarp = BM >= 32 ? BM / 2 : BM;
-    const int chalf = (warp - 2) / 4;
+    // the warps of a TMEM lane quadrant split the BM columns; a 16-column tile stays whole
+    constexpr int kColGroups = BM / 16 < kDequantWarps / 4 ? BM / 16 : kDequantWarps / 4;
+    constexpr int kColsPerWarp = BM / kColGroups;
+    const int chalf = (warp - 2) / 4;   // column group (warps past kColGroups idle here)
     const int n = n0 + row;
     float rs = 1.f;
     if (FMT == LB_FMT_INT8 && p.group == p.k && n < p.n) rs = __half2float(p.scales[n]);
