@@ -357,7 +357,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const int row = 32 * (warp & 3) + lane;          // TMEM lane this warp may access
     // the warps of a TMEM lane quadrant split the BM columns; a 16-column tile stays whole
-    constexpr int kColGroups = BM / 16 < kDequantWarps / 4 ? BM / 16 : kDequantWarps / 4;
+    constexpr int kQuads = kDequantWarps / 4;   // warps per TMEM lane quadrant
+    constexpr int kColGroups = BM / 16 < kQuads ? BM / 16 : (kQuads >= 4 ? 4 : kQuads);   // divides BM / 16
     constexpr int kColsPerWarp = BM / kColGroups;
     const int chalf = (warp - 2) / 4;   // column group (warps past kColGroups idle here)
     const int n = n0 + row;
