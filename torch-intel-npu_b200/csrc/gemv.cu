@@ -520,47 +520,56 @@ __global__ void __launch_bounds__(256) lowrank_project_kernel(int m, int k, int 
 }
 
 // z[m, c] = half(sum_k x[m,k] V[c,k]) for prefill batches (M > 64): one CTA per 16 activation
-// rows; its 8 warps split K (16-element steps) and each computes the 16 x 32 tile with
+// rows; its kZWarps warps split K in 32-element chunks and each computes the 16 x 32 tile with
 // mma.sync m16n8k16 -- x rows as the A operand, V rows (the correction factor, zero past
-// the rank) as B -- then the warps' fp32 partials are summed in a fixed order.  x is read
-// once; V (rank x K) stays in L1/L2.
-__global__ void __launch_bounds__(256) lowrank_project_mma_kernel(int m, int k, int rank, int zs,
-                                                                  const __half *__restrict__ x,
-                                                                  const __half *__restrict__ v, __half *__restrict__ z) {
-  __shared__ float part[8][16][33];
+// the rank) as B.  Lane (g, t) loads 16 contiguous bytes (elements 8t .. 8t+7 of a chunk)
+// of x rows g and g + 8 and of V rows g + 8 nt: the same K permutation for both operands,
+// so one 16-byte load feeds two k16 tiles.  The warps' fp32 partials are summed in a fixed
+// order.  x is read once; V (rank x K) stays in L1/L2.
+constexpr int kZWarps = 16;
+__global__ void __launch_bounds__(32 * kZWarps) lowrank_project_mma_kernel(int m, int k, int rank, int zs,
+                                                                         const __half *__restrict__ x,
+                                                                         const __half *__restrict__ v,
+                                                                         __half *__restrict__ z) {
+  __shared__ float part[kZWarps][16][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int r0 = blockIdx.x * 16;
+  const int chunks = k / 32;
+  const int c0 = warp * chunks / kZWarps, c1 = (warp + 1) * chunks / kZWarps;
+  const bool ra = r0 + g < m, rb = r0 + g + 8 < m;
+  const __half *xa = x + int64_t(ra ? r0 + g : 0) * k + 8 * t;
+  const __half *xb = x + int64_t(rb ? r0 + g + 8 : 0) * k + 8 * t;
+  const __half *vr[4];
+  bool vok[4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int c = nt * 8 + g;
+    vok[nt] = c < rank;
+    vr[nt] = v + int64_t(vok[nt] ? c : 0) * k + 8 * t;
+  }
   pdl_launch();
   pdl_wait();
-  const int steps = k / 16;
-  const int s0 = warp * steps / 8, s1 = (warp + 1) * steps / 8;
   float acc[4][4];
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-  const bool ra = r0 + g < m, rb = r0 + g + 8 < m;
-  const uint32_t *xa = reinterpret_cast<const uint32_t *>(x + int64_t(ra ? r0 + g : 0) * k);
-  const uint32_t *xb = reinterpret_cast<const uint32_t *>(x + int64_t(rb ? r0 + g + 8 : 0) * k);
-#pragma unroll 2
-  for (int st = s0; st < s1; ++st) {
-    const int kp = st * 8 + t;   // pair index of element 16 st + 2t
-    uint32_t a[4];
-    a[0] = ra ? xa[kp] : 0u;
-    a[1] = rb ? xb[kp] : 0u;
-    a[2] = ra ? xa[kp + 4] : 0u;
-    a[3] = rb ? xb[kp + 4] : 0u;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+#pragma unroll 4
+  for (int ch = c0; ch < c1; ++ch) {
+    const int e = ch * 32;
+    const uint4 qa = ra ? *reinterpret_cast<const uint4 *>(xa + e) : zero;
+    const uint4 qb = rb ? *reinterpret_cast<const uint4 *>(xb + e) : zero;
+    uint4 qv[4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) qv[nt] = vok[nt] ? *reinterpret_cast<const uint4 *>(vr[nt] + e) : zero;
+    const uint32_t a0[4] = {qa.x, qb.x, qa.y, qb.y};   // k positions 2t, 2t+1 | 2t+8, 2t+9 of tile 0
+    const uint32_t a1[4] = {qa.z, qb.z, qa.w, qb.w};   // the same positions of tile 1
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      const int c = nt * 8 + g;
-      uint32_t b0 = 0, b1 = 0;
-      if (c < rank) {
-        const uint32_t *vr = reinterpret_cast<const uint32_t *>(v + int64_t(c) * k);
-        b0 = vr[kp];
-        b1 = vr[kp + 4];
-      }
-      mma16816(acc[nt], a, b0, b1);
+      mma16816(acc[nt], a0, qv[nt].x, qv[nt].y);
+      mma16816(acc[nt], a1, qv[nt].z, qv[nt].w);
     }
   }
 #pragma unroll
@@ -576,7 +585,7 @@ __global__ void __launch_bounds__(256) lowrank_project_mma_kernel(int m, int k, 
     if (r0 + rr >= m) continue;
     float sum = 0.f;
     if (c < 32 && c < rank)
-      for (int w = 0; w < 8; ++w) sum += part[w][rr][c];
+      for (int w = 0; w < kZWarps; ++w) sum += part[w][rr][c];
     z[int64_t(r0 + rr) * zs + c] = __float2half_rn(sum);
   }
 }
@@ -815,8 +824,8 @@ static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_
 cudaError_t launch_lowrank_project(int m, int k, int rank, int zs, const uint16_t *x, const uint16_t *v, uint16_t *z,
                                    cudaStream_t st) {
   const bool vec = k % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(v) & 15u) == 0;
-  if (vec && m > 64 && zs == 32 && k % 16 == 0)
-    return launch_k(lowrank_project_mma_kernel, dim3((m + 15) / 16), dim3(256), 0, st, m, k, rank, zs,
+  if (vec && m > 64 && zs == 32 && k % 32 == 0)
+    return launch_k(lowrank_project_mma_kernel, dim3((m + 15) / 16), dim3(32 * kZWarps), 0, st, m, k, rank, zs,
                     reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
                     reinterpret_cast<__half *>(z));
   if (vec)

@@ -13,7 +13,7 @@
 //     accumulate) and commits to the stage's and the A buffer's "empty" barriers.
 // The rank-32 correction is a second TMEM accumulator: U tile [128 x 32] and z tile
 // [BM x 32] (64-byte swizzle) feed two more MMAs, issued before the main loop (for the
-// dequant formats the two tiles are loaded into the two A buffers, which the dequant
+// dequant formats the two tiles are loaded into the last two A buffers, which the dequant
 // warps take over once those MMAs complete), so delta = z.U^T lands beside y_q.
 // Epilogue (warps 2..5): tcgen05.ld, per-row INT8 scale, y = half(half(acc)+bias),
 // y = half(y + half(delta)), stored transposed to y[m, n].
@@ -93,9 +93,11 @@ template <int FMT, int BM> struct TcLayout {
   static constexpr int LUT_BYTES = FMT == LB_FMT_NF4 ? 256 * 32 * 4 : 0;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + SA * A_BYTES;
-  // U and z: A buffers 0 and 1 for the dequant formats, a region of their own for fp16
-  static constexpr int OFF_A2 = kDeq ? OFF_A : OFF_B + S * B_BYTES;
-  static constexpr int OFF_B2 = kDeq ? OFF_A + A_BYTES : OFF_A2 + A2_BYTES;
+  // U and z: the last two A buffers for the dequant formats (so that the first stage's
+  // dequant need not wait for the correction MMAs), a region of their own for fp16
+  static constexpr int ZSLOT = SA - 2;   // first A buffer holding the correction tiles
+  static constexpr int OFF_A2 = kDeq ? OFF_A + ZSLOT * A_BYTES : OFF_B + S * B_BYTES;
+  static constexpr int OFF_B2 = kDeq ? OFF_A + (ZSLOT + 1) * A_BYTES : OFF_A2 + A2_BYTES;
   static constexpr int OFF_C = (((kDeq ? OFF_B + S * B_BYTES : OFF_B2 + B2_BYTES) + 1023) / 1024) * 1024;
   static constexpr int OFF_LUT = OFF_C + S * C_BYTES;
   static constexpr int OFF_BAR = ((OFF_LUT + LUT_BYTES + 15) / 16) * 16;
@@ -228,9 +230,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t bd = umma_desc(sbase + L::OFF_B2, 512, kSwizzle64);
           umma_f16(tmem_corr, ad, bd, idesc, 0u);
           umma_f16(tmem_corr, ad + 2, bd + 2, idesc, 1u);
-          if (kDequant) {   // U and z sit in A buffers 0 and 1: hand them to the dequant warps
-            umma_commit(bar_empty_a);
-            umma_commit(bar_empty_a + 8);
+          if (kDequant) {   // U and z sit in the last two A buffers: hand them to the dequant warps
+            umma_commit(bar_empty_a + 8 * L::ZSLOT);
+            umma_commit(bar_empty_a + 8 * (L::ZSLOT + 1));
           }
         }
       }
@@ -275,11 +277,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       pdl_wait();
 #pragma unroll
       for (int j = 0; j < kScaleAhead; ++j) ring[j] = load_scale(group + kStageGroups * j);
-      // uses of A buffer a: the correction tiles (buffers 0 and 1, if any), then the main
-      // stages i = a, a + SA, ...
+      // uses of A buffer a: the correction tiles (the last two buffers, if any), then the
+      // main stages i = a, a + SA, ...
       for (int i = group; i < nst; i += kStageGroups) {
         const int s = i % S, a = i % SA;
-        const int first_use = corr && a < 2 ? 1 : 0;
+        const int first_use = corr && a >= L::ZSLOT ? 1 : 0;
         const __half2 sc = ring[0];
 #pragma unroll
         for (int j = 0; j + 1 < kScaleAhead; ++j) ring[j] = ring[j + 1];
