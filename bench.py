@@ -147,11 +147,19 @@ def capture_steps(cells, stream):
 
 
 def launches_per_step(cells):
+    """Kernel launches of one sweep step.  A corrected decode GEMV (M <= 16, rank <= 32)
+    with >= 4 MiB of codes computes its z projection inside the same launch (the rule of
+    launch_gemv_fused_z in csrc/gemv.cu; the sweep's grids always fit the device at once);
+    otherwise the projection is a launch of its own."""
     import lowbit_runtime as rt
     count = 0
     for c in cells:
         path = rt.linear_select(c['fmt'], c['g'], 1, c['n'], c['k'], RANK)
-        count += 2 if path in ('gemv', 'generic') else 3   # z projection + linear (+ finalize)
+        code_bytes = c['n'] * c['k'] * (8 if c['fmt'] == 'int8' else 4) // 8
+        if path == 'gemv' and RANK <= 32 and code_bytes >= (4 << 20):
+            count += 1
+        else:
+            count += 2 if path in ('gemv', 'generic') else 3   # z projection + linear (+ finalize)
     return count
 
 
@@ -237,7 +245,7 @@ def prefill_roofline(device, stream, peak_tf):
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel (mean of
 # the two captured launches), from the committed ncu capture
 # (profiles/gemv_nf4_g64_8192x2048_m1.md).
-TRAFFIC_PER_LAUNCH = {DOMINANT: 8976256}
+TRAFFIC_PER_LAUNCH = {DOMINANT: 8983552}
 
 
 def cpu_reference_sweep(sample_cells, reps):
