@@ -293,13 +293,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint8_t *abuf = smem + L::OFF_A + a * L::A_BYTES;
         if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
           constexpr int W = EPP / 8;   // 32-bit code words (8 codes each) of this part
+          static_assert(W == 4, "one 16-byte chunk of codes per thread and stage");
           uint32_t wv[W];
-          if constexpr (W == 4) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * part);
+          {
+            // the code tile arrives 32B-swizzled: chunk c of row r sits at c ^ ((r >> 2) & 1),
+            // so the lanes' 16-byte reads (32 consecutive rows) cover all bank groups
+            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * (part ^ ((drow >> 2) & 1)));
             wv[0] = c.x; wv[1] = c.y; wv[2] = c.z; wv[3] = c.w;
-          } else {
-            const uint2 c = *reinterpret_cast<const uint2 *>(crow + 8 * part);
-            wv[0] = c.x; wv[1] = c.y;
           }
 #pragma unroll
           for (int w = 0; w < W; ++w) {
@@ -327,7 +327,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           uint32_t wv[4 * V];
 #pragma unroll
           for (int v = 0; v < V; ++v) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(crow + EPP * part + 16 * v);
+            // 64B-swizzled code tile: chunk c of row r sits at c ^ ((r >> 1) & 3)
+            const uint4 c = *reinterpret_cast<const uint4 *>(crow + 16 * ((EPP / 16 * part + v) ^ ((drow >> 1) & 3)));
             wv[4 * v] = c.x; wv[4 * v + 1] = c.y; wv[4 * v + 2] = c.z; wv[4 * v + 3] = c.w;
           }
 #pragma unroll
@@ -543,7 +544,7 @@ cudaError_t launch_tc(int fmt, int group, int m, int n, int k, const uint16_t *x
   else {
     const uint64_t rb = fmt == LB_FMT_INT8 ? uint64_t(k) : uint64_t(k) / 2;
     ok = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, rb, n, rb, fmt == LB_FMT_INT8 ? 64 : 32, 128,
-                  CU_TENSOR_MAP_SWIZZLE_NONE);
+                  fmt == LB_FMT_INT8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
   }
   ok = ok && make_map(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m, uint64_t(k) * 2, 64, bm, CU_TENSOR_MAP_SWIZZLE_128B);
   const bool corr = z != nullptr;
