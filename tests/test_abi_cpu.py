@@ -68,6 +68,30 @@ def test_validation_rejects_before_any_launch(lib):
     assert lib.lb_quantize_pack(0, 16, P(16), 1, 2, 16, P(16), P(16), None, 0, None) == 6
 
 
+def test_fast_call_module_matches_the_ctypes_binding(lib):
+    """lowbit_runtime.linear calls lb_linear_path through the _lowbit_call module (plain C
+    over the same entry point of the same loaded library); on host-validated inputs it
+    returns exactly the statuses the ctypes binding returns, and rejects malformed calls."""
+    import lowbit_runtime as rt
+    fast = rt._FAST_LINEAR
+    assert fast is not None, '_lowbit_call was not built beside liblowbit.so'
+    cases = [
+        (0, 9, 64, 1, 8, 64, 16, 16, 16, None, None, 0, None, 16, 16, 4096, None),           # bad format
+        (0, 0, 3, 1, 8, 64, 16, 16, 16, None, None, 0, None, 16, 16, 4096, None),            # bad group
+        (0, 0, 64, 0, 8, 64, 16, 16, 16, None, None, 0, None, 16, 16, 4096, None),           # M = 0
+        (0, 0, 64, 1, 8, 64, 16, 16, 16, 16, None, 32, None, 16, 16, 4096, None),            # unpaired factors
+        (0, 0, 64, 1, 8, 64, 16, 4096, 8192, None, None, 0, None, 1 << 20, 1 << 24, 8, None),  # workspace
+        (0, 0, 64, 1, 8, 64, 1 << 20, 4096, 8192, None, None, 0, None, 1 << 20, 1 << 24, 1 << 16, None),  # alias
+        (0, 0, 64, 1, 8, 64, 1 << 47, 1 << 46, 1 << 45, None, None, 0, None, 1 << 47, 1 << 44, 4, 0),
+    ]
+    for args in cases:
+        assert fast(*args) == lib.lb_linear_path(*args), args
+    with pytest.raises(TypeError):
+        fast(0, 0, 64)
+    with pytest.raises(OverflowError):
+        fast(0, 1 << 40, 64, 1, 8, 64, 16, 16, 16, None, None, 0, None, 16, 16, 4096, None)
+
+
 def test_path_selection():
     import lowbit_runtime as rt
     assert rt.linear_select('nf4', 64, 1, 8192, 2048) == 'gemv'

@@ -7,11 +7,14 @@ import hashlib
 import os
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
 OUT = HERE / 'liblowbit.so'
+# CPython fast path for the per-call entry point (plain C over the C ABI, see csrc/pycall.c)
+PYCALL_OUT = HERE / ('_lowbit_call' + (sysconfig.get_config_var('EXT_SUFFIX') or '.so'))
 INCLUDE = HERE.parent / 'include'
 SOURCES = ['abi.cu', 'quantize.cu', 'gemv.cu', 'tc_gemm.cu', 'decoder_ops.cu', 'noalloc.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
@@ -32,7 +35,7 @@ def _digest():
 def build(force=False, verbose=False):
     stamp = HERE / '.liblowbit.sha256'
     digest = _digest()
-    if not force and OUT.exists() and stamp.exists() and stamp.read_text() == digest:
+    if not force and OUT.exists() and PYCALL_OUT.exists() and stamp.exists() and stamp.read_text() == digest:
         return OUT
     cmd = [NVCC, *FLAGS, '-I', str(INCLUDE), *[str(CSRC / s) for s in SOURCES], '-o', str(OUT) + '.tmp']
     if verbose:
@@ -43,6 +46,12 @@ def build(force=False, verbose=False):
     if verbose:
         print(r.stdout + r.stderr)
     os.replace(str(OUT) + '.tmp', OUT)
+    cc = os.environ.get('CC', 'gcc')
+    r = subprocess.run([cc, '-O2', '-shared', '-fPIC', '-I', sysconfig.get_paths()['include'], str(CSRC / 'pycall.c'),
+                        '-o', str(PYCALL_OUT) + '.tmp'], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError('building the _lowbit_call module failed:\n' + r.stdout + r.stderr)
+    os.replace(str(PYCALL_OUT) + '.tmp', PYCALL_OUT)
     stamp.write_text(digest)
     return OUT
 

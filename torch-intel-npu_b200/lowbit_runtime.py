@@ -73,8 +73,32 @@ def load_library():
                 fn = getattr(lib, name)
                 fn.argtypes = args
                 fn.restype = res
+            _bind_fast_call(lib)
             _LIB = lib
     return _LIB
+
+
+# lb_linear_path through the _lowbit_call module (built beside liblowbit.so): the same C
+# entry point of the same loaded library, without ctypes' per-argument conversion.  When
+# the module is absent the ctypes binding is used.
+_FAST_LINEAR = None
+
+
+def _bind_fast_call(lib):
+    global _FAST_LINEAR
+    try:
+        import _lowbit_call
+    except ImportError:
+        _FAST_LINEAR = None
+        return
+    _lowbit_call.bind(ctypes.cast(lib.lb_linear_path, ctypes.c_void_p).value)
+    _FAST_LINEAR = _lowbit_call.linear_path
+
+
+def _current_stream(dev):
+    """Raw handle of torch's current stream on CUDA device ``dev``."""
+    get = getattr(torch._C, '_cuda_getCurrentRawStream', None)
+    return get(dev.index) if get is not None else torch.cuda.current_stream(dev).cuda_stream
 
 
 def lib():
@@ -225,11 +249,11 @@ def linear(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, ou
     fmt_id = LB_FMT[fmt]
     dev = x.device
     y = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=dev)
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = _current_stream(dev)
     ws = Workspace.for_stream(_linear_ws_bytes(fmt_id, group, m, n, k, rank), dev.index, stream)
-    status = L.lb_linear_path(PATH[path], fmt_id, group, m, n, k, x.data_ptr(), codes.data_ptr(), _addr(scales),
-                              _addr(down), _addr(up), rank, _addr(bias), y.data_ptr(), ws.data_ptr(), ws.numel(),
-                              stream)
+    call = _FAST_LINEAR if _FAST_LINEAR is not None else L.lb_linear_path
+    status = call(PATH[path], fmt_id, group, m, n, k, x.data_ptr(), codes.data_ptr(), _addr(scales), _addr(down),
+                  _addr(up), rank, _addr(bias), y.data_ptr(), ws.data_ptr(), ws.numel(), stream)
     if status != OK:
         check(status, 'lb_linear')
     return y
