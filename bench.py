@@ -293,20 +293,20 @@ def e2e_block(cells, steps, warmup, device, stream):
     host_y = torch.empty(total_n, dtype=torch.float16).pin_memory()
     dev_x = torch.empty(total_k, dtype=torch.float16, device=device)
     dev_y = torch.empty(total_n, dtype=torch.float16, device=device)
-    offs_k, offs_n, a, b = [], [], 0, 0
+    # each cell's activation / output rows are fixed views into the staging buffers (made once,
+    # as a caller's preallocated buffers would be); every step copies the host activations in
+    # and the outputs back out
+    views, a, b = [], 0, 0
     for c in cells:
-        offs_k.append(a)
-        offs_n.append(b)
+        views.append((dev_x[a:a + c['k']].view(1, c['k']), dev_y[b:b + c['n']].view(1, c['n'])))
         a += c['k']
         b += c['n']
 
     def step(i):
         r = i % REPLICAS
         dev_x.copy_(host_x, non_blocking=True)
-        for j, c in enumerate(cells):
+        for c, (x, y) in zip(cells, views):
             codes, scales = c['reps'][r]
-            x = dev_x[offs_k[j]:offs_k[j] + c['k']].view(1, c['k'])
-            y = dev_y[offs_n[j]:offs_n[j] + c['n']].view(1, c['n'])
             rt.linear(x, c['fmt'], c['g'], c['n'], codes, scales, down=c['v'], up=c['u'], out=y)
         host_y.copy_(dev_y, non_blocking=True)
 
