@@ -186,6 +186,23 @@ def test_gemv_work_splits_agree(rt, monkeypatch, plan, fmt, g, m):
     assert torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize('fmt,g', [('nf4', 128), ('int4', 64)])
+@pytest.mark.parametrize('m', [4096, 4133])
+def test_prefill_batches_from_4096_rows_match_oracle(rt, fmt, g, m):
+    """From 4096 activation rows the correction's projection runs with two m16 tiles per
+    CTA (ragged M included); the tcgen05 result with correction matches the oracle."""
+    n, k = 576, 1536
+    w, u, v = baseline_weight(n, k, seed=41)
+    group, data, scales = ref.quantize(w.numpy(), fmt, g)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(42)).half()
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    assert rt.linear_select(fmt, group, m, n, k, 32) == 'tc'
+    expected = _oracle(x, (n, k), fmt, group, data, scales, down=v, up=u)
+    y = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda())
+    _compare(y, expected, (fmt, g, m))
+
+
 def test_large_prefill_shape_properties(rt):
     """Full BASELINE prefill size: deterministic, zero-in gives the correction-free zero,
     and a row sample matches the oracle."""

@@ -519,27 +519,37 @@ __global__ void __launch_bounds__(256) lowrank_project_kernel(int m, int k, int 
   }
 }
 
-// z[m, c] = half(sum_k x[m,k] V[c,k]) for prefill batches (M > 64): one CTA per 16 activation
-// rows; its kZWarps warps split K in 32-element chunks and each computes the 16 x 32 tile with
-// mma.sync m16n8k16 -- x rows as the A operand, V rows (the correction factor, zero past
-// the rank) as B.  Lane (g, t) loads 16 contiguous bytes (elements 8t .. 8t+7 of a chunk)
-// of x rows g and g + 8 and of V rows g + 8 nt: the same K permutation for both operands,
-// so one 16-byte load feeds two k16 tiles.  The warps' fp32 partials are summed in a fixed
-// order.  x is read once; V (rank x K) stays in L1/L2.
+// z[m, c] = half(sum_k x[m,k] V[c,k]) for prefill batches (M > 64): one CTA per MT m16 tiles of
+// activation rows (two from 4096 rows on: they share every V load, and at that size the grid
+// still fills the device); its kZWarps warps split K in 32-element
+// chunks and each computes the 32 x 32 tile with mma.sync m16n8k16 -- x rows as the A
+// operand, V rows (the correction factor, zero past the rank) as B.  Lane (g, t) loads 16
+// contiguous bytes (elements 8t .. 8t+7 of a chunk) of x rows g, g + 8 (+16 for the second
+// tile) and of V rows g + 8 nt: the same K permutation for both operands, so one 16-byte
+// load feeds two k16 tiles.  The warps' fp32 partials are summed in a fixed order (shared
+// memory [warps][16 MT][33], dynamic).  x is read once; V (rank x K) stays in L1/L2.
 constexpr int kZWarps = 16;
+template <int MT> constexpr int z_smem_bytes() { return kZWarps * 16 * MT * 33 * 4; }
+template <int MT>
 __global__ void __launch_bounds__(32 * kZWarps) lowrank_project_mma_kernel(int m, int k, int rank, int zs,
                                                                          const __half *__restrict__ x,
                                                                          const __half *__restrict__ v,
                                                                          __half *__restrict__ z) {
-  __shared__ float part[kZWarps][16][33];
+  constexpr int kZRows = 16 * MT;
+  extern __shared__ float part[];   // [kZWarps][kZRows][33]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int r0 = blockIdx.x * 16;
+  const int r0 = blockIdx.x * kZRows;
   const int chunks = k / 32;
   const int c0 = warp * chunks / kZWarps, c1 = (warp + 1) * chunks / kZWarps;
-  const bool ra = r0 + g < m, rb = r0 + g + 8 < m;
-  const __half *xa = x + int64_t(ra ? r0 + g : 0) * k + 8 * t;
-  const __half *xb = x + int64_t(rb ? r0 + g + 8 : 0) * k + 8 * t;
+  const __half *xr[2 * MT];
+  bool rok[2 * MT];
+#pragma unroll
+  for (int j = 0; j < 2 * MT; ++j) {   // rows g, g + 8 (, g + 16, g + 24)
+    const int row = r0 + g + 8 * j;
+    rok[j] = row < m;
+    xr[j] = x + int64_t(rok[j] ? row : 0) * k + 8 * t;
+  }
   const __half *vr[4];
   bool vok[4];
 #pragma unroll
@@ -550,42 +560,51 @@ __global__ void __launch_bounds__(32 * kZWarps) lowrank_project_mma_kernel(int m
   }
   pdl_launch();
   pdl_wait();
-  float acc[4][4];
+  float acc[MT][4][4];
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
   const uint4 zero = make_uint4(0, 0, 0, 0);
-#pragma unroll 4
+#pragma unroll 2
   for (int ch = c0; ch < c1; ++ch) {
     const int e = ch * 32;
-    const uint4 qa = ra ? *reinterpret_cast<const uint4 *>(xa + e) : zero;
-    const uint4 qb = rb ? *reinterpret_cast<const uint4 *>(xb + e) : zero;
-    uint4 qv[4];
+    uint4 q[2 * MT], qv[4];
+#pragma unroll
+    for (int j = 0; j < 2 * MT; ++j) q[j] = rok[j] ? *reinterpret_cast<const uint4 *>(xr[j] + e) : zero;
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) qv[nt] = vok[nt] ? *reinterpret_cast<const uint4 *>(vr[nt] + e) : zero;
-    const uint32_t a0[4] = {qa.x, qb.x, qa.y, qb.y};   // k positions 2t, 2t+1 | 2t+8, 2t+9 of tile 0
-    const uint32_t a1[4] = {qa.z, qb.z, qa.w, qb.w};   // the same positions of tile 1
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      mma16816(acc[nt], a0, qv[nt].x, qv[nt].y);
-      mma16816(acc[nt], a1, qv[nt].z, qv[nt].w);
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint4 qa = q[2 * mt], qb = q[2 * mt + 1];
+      const uint32_t a0[4] = {qa.x, qb.x, qa.y, qb.y};   // k positions 2t, 2t+1 | 2t+8, 2t+9 of tile 0
+      const uint32_t a1[4] = {qa.z, qb.z, qa.w, qb.w};   // the same positions of tile 1
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        mma16816(acc[mt][nt], a0, qv[nt].x, qv[nt].y);
+        mma16816(acc[mt][nt], a1, qv[nt].z, qv[nt].w);
+      }
     }
   }
+  float *pw = part + warp * kZRows * 33;
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-    part[warp][g][nt * 8 + 2 * t] = acc[nt][0];
-    part[warp][g][nt * 8 + 2 * t + 1] = acc[nt][1];
-    part[warp][g + 8][nt * 8 + 2 * t] = acc[nt][2];
-    part[warp][g + 8][nt * 8 + 2 * t + 1] = acc[nt][3];
-  }
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      pw[(16 * mt + g) * 33 + nt * 8 + 2 * t] = acc[mt][nt][0];
+      pw[(16 * mt + g) * 33 + nt * 8 + 2 * t + 1] = acc[mt][nt][1];
+      pw[(16 * mt + g + 8) * 33 + nt * 8 + 2 * t] = acc[mt][nt][2];
+      pw[(16 * mt + g + 8) * 33 + nt * 8 + 2 * t + 1] = acc[mt][nt][3];
+    }
   __syncthreads();
-  for (int i = threadIdx.x; i < 16 * zs; i += blockDim.x) {
+  for (int i = threadIdx.x; i < kZRows * zs; i += blockDim.x) {
     const int rr = i / zs, c = i % zs;
     if (r0 + rr >= m) continue;
     float sum = 0.f;
     if (c < 32 && c < rank)
-      for (int w = 0; w < kZWarps; ++w) sum += part[w][rr][c];
+      for (int w = 0; w < kZWarps; ++w) sum += part[(w * kZRows + rr) * 33 + c];
     z[int64_t(r0 + rr) * zs + c] = __float2half_rn(sum);
   }
 }
@@ -824,10 +843,17 @@ static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_
 cudaError_t launch_lowrank_project(int m, int k, int rank, int zs, const uint16_t *x, const uint16_t *v, uint16_t *z,
                                    cudaStream_t st) {
   const bool vec = k % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(v) & 15u) == 0;
-  if (vec && m > 64 && zs == 32 && k % 32 == 0)
-    return launch_k(lowrank_project_mma_kernel, dim3((m + 15) / 16), dim3(32 * kZWarps), 0, st, m, k, rank, zs,
-                    reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
-                    reinterpret_cast<__half *>(z));
+  if (vec && m > 64 && zs == 32 && k % 32 == 0) {
+    auto go = [&](auto kern, int rows, int smem) -> cudaError_t {
+      const cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), smem);
+      if (e != cudaSuccess) return e;
+      return launch_k(kern, dim3((m + rows - 1) / rows), dim3(32 * kZWarps), size_t(smem), st, m, k, rank, zs,
+                      reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
+                      reinterpret_cast<__half *>(z));
+    };
+    return m >= 4096 ? go(lowrank_project_mma_kernel<2>, 32, z_smem_bytes<2>())
+                     : go(lowrank_project_mma_kernel<1>, 16, z_smem_bytes<1>());
+  }
   if (vec)
     return launch_k(lowrank_project_kernel, dim3(zs, (m + 7) / 8), dim3(256), 0, st, m, k, rank, zs,
                     reinterpret_cast<const __half *>(x), reinterpret_cast<const __half *>(v),
