@@ -203,25 +203,27 @@ def dominant_kernel_roofline(device, stream, peak_gbs):
     return {'kernel': 'gemv_kernel<NF4> (8192x2048, group 64, M=1)', 'bound': 'hbm', 'achieved': round(achieved, 1),
             'peak': peak_gbs, 'unit': 'GB/s', 'frac': round(achieved / peak_gbs, 4), 'launch_us': round(t * 1e6, 3),
             'bytes_per_launch': per_launch,
-            'traffic': TRAFFIC_PER_LAUNCH.get(DOMINANT)}
+            'traffic': TRAFFIC_PER_LAUNCH.get(DOMINANT),
+            'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of bench.py --profile dominant'}
 
 
-PREFILL = ('nf4', 64, 8192, 2048, 8192)   # the 1.7B gate/up shape at a prefill batch of 8192 tokens
+PREFILL_SHAPE = ('nf4', 64, 8192, 2048)   # the 1.7B gate/up projection
+PREFILL_MS = (2048, 8192, 65536)           # configs[1]'s largest M, a mid batch, configs[4]'s 32 x 2048 tokens
 
 
-def prefill_roofline(device, stream, peak_tf):
+def prefill_roofline(device, stream, peak_tf, m):
     """The prefill GEMM on the tensor cores: NF4 g64 8192x2048 with the rank-32 correction
-    at M=8192 (tcgen05 path, z projection included), back to back in one graph over two
-    weight replicas; achieved = FLOPs per call / duration vs the measured bf16 peak."""
+    (tcgen05 path, z projection included), back to back in one graph over two weight
+    replicas; achieved = FLOPs per call / duration vs the measured bf16 peak."""
     import lowbit_runtime as rt
-    fmt, g, n, k, m = PREFILL
+    fmt, g, n, k = PREFILL_SHAPE
     gen = torch.Generator(device='cpu').manual_seed(2)
     reps = [rt.quantize_pack((torch.randn(n, k, generator=gen) * 0.02).half().to(device), fmt, g) for _ in range(2)]
     x = torch.randn(m, k, generator=gen).half().to(device)
     v = (torch.randn(RANK, k, generator=gen) * 1e-3).half().to(device)
     u = (torch.randn(n, RANK, generator=gen) * 1e-3).half().to(device)
     y = torch.empty(m, n, dtype=torch.float16, device=device)
-    launches = 8
+    launches = 8 if m <= 8192 else 4
     with torch.cuda.stream(stream):
         for c, sc in reps:
             rt.linear(x, fmt, g, n, c, sc, down=v, up=u, out=y)
@@ -234,23 +236,23 @@ def prefill_roofline(device, stream, peak_tf):
             graph.replay()
         stream.synchronize()
         t = timed(lambda i: graph.replay(), 3, stream) / (3 * launches)
-    flops = 2 * m * n * k + 2 * m * RANK * (n + k)
+    flops = gemm_flops(m, n, k)
     achieved = flops / t / 1e12
-    return {'kernel': 'tc_linear_kernel<NF4, 256> (+ z projection), 8192x2048, group 64, M=8192, rank 32',
+    del graph, x, y, reps
+    return {'kernel': f'tc_linear_kernel<NF4> (+ z projection), 8192x2048, group 64, M={m}, rank 32',
             'bound': 'tensor', 'achieved': round(achieved, 1), 'peak': peak_tf, 'unit': 'TFLOP/s',
-            'frac': round(achieved / peak_tf, 4), 'launch_us': round(t * 1e6, 2), 'flops_per_call': flops,
-            'tensor_pipe_active': 'profiles/tc_linear_nf4_g64_m2048_8192x2048.md'}
+            'frac': round(achieved / peak_tf, 4), 'launch_us': round(t * 1e6, 2), 'flops_per_call': flops}
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel (mean of
-# the two captured launches), from the committed ncu capture
-# (profiles/gemv_nf4_g64_8192x2048_m1.md).
+# the captured launches), from an ncu capture of `bench.py --profile dominant`.
 TRAFFIC_PER_LAUNCH = {DOMINANT: 8983552}
 
 
-def cpu_reference_sweep(sample_cells, reps):
+def cpu_reference_sweep(sample_cells, reps, cached=False):
     """The reference's CPU staging on a bounded sample: per call dequantize + fp32 linear +
-    correction (torch_npu_smollm.py:150-164 via the oracle restatement)."""
+    correction (torch_npu_smollm.py:150-164 via the oracle restatement); with ``cached``
+    the dequantized weight is computed once and reused (torch_npu_lowbit_demo.py:65-71)."""
     from oracle import lowbit_ref as ref
     gen = torch.Generator().manual_seed(0)
     prepared = []
@@ -260,32 +262,155 @@ def cpu_reference_sweep(sample_cells, reps):
         v = (torch.randn(RANK, k, generator=gen) * 1e-3).half()
         group, data, scales = ref.quantize(w.numpy(), fmt, g)
         x = torch.randn(1, k, generator=gen).half()
-        prepared.append((fmt, group, n, k, data, scales, u, v, x))
+        wp = ref.prepare_weight((n, k), fmt, group, data, scales) if cached else None
+        prepared.append((fmt, group, n, k, data, scales, u, v, x, wp))
     total_bytes = 0
     t0 = time.perf_counter()
     for _ in range(reps):
-        for fmt, group, n, k, data, scales, u, v, x in prepared:
-            ref.linear(x, (n, k), fmt, group, data, scales, down=v, up=u)
+        for fmt, group, n, k, data, scales, u, v, x, wp in prepared:
+            if wp is None:
+                ref.linear(x, (n, k), fmt, group, data, scales, down=v, up=u)
+            else:
+                ref.linear_prepared(x, wp, down=v, up=u)
             total_bytes += gemv_bytes(1, n, k, fmt, group)
     dt = time.perf_counter() - t0
     return total_bytes / dt / 1e9, dt
 
 
-def cpu_baseline_block(budget_s=12.0):
+def cpu_decode_baseline(budget_s=8.0):
+    """Decode on the host cores through the oracle restatement of reference_cpu
+    (torch_npu_smollm.py:142-193, per-call dequantization) and FrozenSmolIO.logits.
+    configs[2] runs whole (30 layers, batch 1, prompt 128, then greedy steps until
+    ``budget_s``); configs[3] and [4] time one layer's decode step at their batch over a
+    random KV cache of their prompt length plus the tied LM head, and extrapolate to all
+    layers (configs[4]'s prefill: one layer over a 256-token prompt, scaled linearly to
+    32 x 2048 tokens and 24 layers, which leaves out attention's quadratic part)."""
+    import torch_npu_smollm as sm
+    from oracle import decoder_ref as dref
+    from oracle import lowbit_ref as ref
+    out = {}
+
+    def dims(name):
+        c = SMOL[name]
+        return dref.DecoderDims(hidden=c['hidden_size'], intermediate=c['intermediate_size'],
+                                heads=c['num_attention_heads'], kv_heads=c['num_key_value_heads'],
+                                vocab=c['vocab_size'], theta=c['rope_theta'])
+
+    def layer(name, mode, group, seed):
+        d = dims(name)
+        gen = torch.Generator().manual_seed(seed)
+        w, packed, corr = {}, {}, {}
+        for pname, (sh, fmt, g) in projection_formats(name, mode, group).items():
+            w[pname] = (torch.randn(sh, generator=gen) * 0.02).half()
+            gg, data, scales = ref.quantize(w[pname].numpy(), fmt, None if fmt == 'int8' else g)
+            packed[pname] = (sh, fmt, gg, data, scales)
+            corr[pname] = ((torch.randn(RANK, sh[1], generator=gen) * 1e-3).half(),
+                           (torch.randn(sh[0], RANK, generator=gen) * 1e-3).half())
+        for nname in ('input_layernorm.weight', 'post_attention_layernorm.weight'):
+            w[nname] = torch.ones(d.hidden, dtype=torch.float16)
+        return dref.LayerRef(d, w, packed, corr)
+
+    def head_time(name, batch):
+        d = dims(name)
+        emb = (torch.randn(d.vocab, d.hidden, generator=torch.Generator().manual_seed(1)) * 0.02).half()
+        dec = dref.DecoderRef(d, [], emb, torch.ones(d.hidden, dtype=torch.float16), 8)
+        h = torch.randn(batch, 1, d.hidden).half()
+        t0 = time.perf_counter()
+        dec.logits(h)
+        return time.perf_counter() - t0
+
+    # configs[2]: the whole 135M model, batch 1
+    d = dims('135m')
+    layers = [layer('135m', 'w8a16', None, 10 + i) for i in range(SMOL['135m']['num_hidden_layers'])]
+    emb = (torch.randn(d.vocab, d.hidden, generator=torch.Generator().manual_seed(2)) * 0.02).half()
+    model = dref.DecoderRef(d, layers, emb, torch.ones(d.hidden, dtype=torch.float16), 128 + 64)
+    ids = torch.randint(0, d.vocab, (1, 128), generator=torch.Generator().manual_seed(3))
+    t0 = time.perf_counter()
+    hidden, caches = model.step(model.embed(ids), None)
+    token = model.logits(hidden[:, -1:])[:, 0].float().argmax(-1)
+    pre = time.perf_counter() - t0
+    steps, t0 = 0, time.perf_counter()
+    while steps < 64 and (steps < 2 or time.perf_counter() - t0 < budget_s):
+        hidden, caches = model.step(model.embed(token[:, None]), caches)
+        token = model.logits(hidden[:, -1:])[:, 0].float().argmax(-1)
+        steps += 1
+    dec = time.perf_counter() - t0
+    out['smollm135m_w8_b1'] = {'tokens_per_s': round(steps / dec, 2), 'prefill_ms': round(pre * 1e3, 1),
+                               'sample': f'whole model, prompt 128, {steps} greedy steps timed'}
+    del layers, model, caches
+
+    def one_layer_decode(name, mode, group, batch, prompt, tag):
+        d = dims(name)
+        lay = layer(name, mode, group, 20)
+        gen = torch.Generator().manual_seed(4)
+        cache = ((torch.randn(batch, d.kv_heads, prompt, d.head_dim, generator=gen) * 0.5).half(),
+                 (torch.randn(batch, d.kv_heads, prompt, d.head_dim, generator=gen) * 0.5).half())
+        cos, sin = dref.rope_tables(d, prompt + 4)
+        x = torch.randn(batch, 1, d.hidden, generator=gen).half()
+        lay.forward(x, cos, sin, cache)                    # warm-up
+        t0 = time.perf_counter()
+        for _ in range(2):
+            lay.forward(x, cos, sin, cache)
+        t_layer = (time.perf_counter() - t0) / 2
+        n_layers = SMOL[name]['num_hidden_layers']
+        step = n_layers * t_layer + head_time(name, batch)
+        out[tag] = {'tokens_per_s': round(batch / step, 3), 'layer_step_ms': round(t_layer * 1e3, 1),
+                    'sample': f'1 layer x 2 decode steps at batch {batch} over a {prompt}-position cache, '
+                              f'extrapolated to {n_layers} layers + LM head'}
+        return lay
+
+    one_layer_decode('360m', 'w4a16', int4_groups(SMOL['360m']), 64, 512, 'smollm360m_int4_b64')
+    one_layer_decode('360m', 'nf4a16', 64, 64, 512, 'smollm360m_nf4g64_b64')
+    lay = one_layer_decode('1.7b', 'nf4a16', 64, 32, 2048, 'smollm1.7b_nf4g64_b32')
+    d = dims('1.7b')
+    cos, sin = dref.rope_tables(d, 260)
+    x = torch.randn(1, 256, d.hidden, generator=torch.Generator().manual_seed(5)).half()
+    t0 = time.perf_counter()
+    lay.forward(x, cos, sin)
+    t_pre = time.perf_counter() - t0
+    total = t_pre * (32 * 2048 / 256) * SMOL['1.7b']['num_hidden_layers']
+    out['smollm1.7b_nf4g64_b32']['prefill_ms_extrapolated'] = round(total * 1e3, 1)
+    out['smollm1.7b_nf4g64_b32']['prefill_sample'] = '1 layer over a 256-token prompt, x 256 and x 24 layers'
+    return out
+
+
+def cpu_baseline_block(budget_s=12.0, decode=True):
     sample = CELLS
     # one untimed pass to size the sample, then enough passes for ~budget_s
     _, dt = cpu_reference_sweep(sample, 1)
     reps = max(1, int(budget_s / max(dt, 1e-3)))
     gbs, dt = cpu_reference_sweep(sample, reps)
-    return {'value': round(gbs, 3), 'unit': 'GB/s', 'cores': torch.get_num_threads(), 'kind': 'port',
-            'sample': f'{reps} pass(es) over all {len(sample)} sweep cells at M=1 with rank-32 correction, '
-                      f'{dt:.1f} s of CPU work (oracle restatement of reference_cpu: dequantize + fp32 linear per call)'}
+    _, dtc = cpu_reference_sweep(sample, 1, cached=True)
+    reps_c = max(1, int(budget_s / 2 / max(dtc, 1e-3)))
+    gbs_c, dtc = cpu_reference_sweep(sample, reps_c, cached=True)
+    out = {'value': round(gbs, 3), 'unit': 'GB/s', 'cores': torch.get_num_threads(), 'host_cpus': os.cpu_count(),
+           'kind': 'port',
+           'sample': f'{reps} pass(es) over all {len(sample)} sweep cells at M=1 with rank-32 correction, '
+                     f'{dt:.1f} s of CPU work (oracle restatement of reference_cpu: dequantize + fp32 linear per call)',
+           'cached_dequant': {'value': round(gbs_c, 3), 'unit': 'GB/s',
+                              'sample': f'{reps_c} pass(es), dequantized weights computed once and reused '
+                                        f'(torch_npu_lowbit_demo.py:65-71), {dtc:.1f} s'}}
+    if decode:
+        out['decode'] = cpu_decode_baseline()
+    return out
 
 
 def e2e_block(cells, steps, warmup, device, stream):
-    """Public API path: QuantizedLinear-equivalent calls with host activations in, host outputs out."""
-    import torch_npu_lowbit as lb  # noqa: F401  (public module; rt.linear is QuantizedLinear.forward's call)
-    import lowbit_runtime as rt
+    """The sweep through the public module, QuantizedLinear.forward (torch_npu_lowbit.py:339
+    in the reference), one module per cell and replica built from the packed bytes and
+    its LowRankCorrection.  Every step copies that step's activations from pinned host
+    memory to the device, runs every cell's forward, and copies all outputs back."""
+    import torch_npu_lowbit as lb
+    from torch_npu_lowbit_correction import LowRankCorrection
+    modules = []
+    for c in cells:
+        corr = LowRankCorrection.from_tensors(c['v'].cpu(), c['u'].cpu())
+        reps = []
+        for codes, scales in c['reps']:
+            pw = lb.PackedWeight((c['n'], c['k']), c['fmt'], c['g'], codes.cpu().numpy().tobytes(),
+                                 scales.cpu().numpy().tobytes())
+            reps.append(lb.QuantizedLinear(pw, correction=corr, device=device))
+        modules.append(reps)
     xs = [c['x'].cpu() for c in cells]
     total_k = sum(x.numel() for x in xs)
     total_n = sum(c['n'] for c in cells)
@@ -294,8 +419,7 @@ def e2e_block(cells, steps, warmup, device, stream):
     dev_x = torch.empty(total_k, dtype=torch.float16, device=device)
     dev_y = torch.empty(total_n, dtype=torch.float16, device=device)
     # each cell's activation / output rows are fixed views into the staging buffers (made once,
-    # as a caller's preallocated buffers would be); every step copies the host activations in
-    # and the outputs back out
+    # as a caller's preallocated buffers would be)
     views, a, b = [], 0, 0
     for c in cells:
         views.append((dev_x[a:a + c['k']].view(1, c['k']), dev_y[b:b + c['n']].view(1, c['n'])))
@@ -305,9 +429,8 @@ def e2e_block(cells, steps, warmup, device, stream):
     def step(i):
         r = i % REPLICAS
         dev_x.copy_(host_x, non_blocking=True)
-        for c, (x, y) in zip(cells, views):
-            codes, scales = c['reps'][r]
-            rt.linear(x, c['fmt'], c['g'], c['n'], codes, scales, down=c['v'], up=c['u'], out=y)
+        for mods, (x, y) in zip(modules, views):
+            mods[r](x, out=y)
         host_y.copy_(dev_y, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -316,8 +439,55 @@ def e2e_block(cells, steps, warmup, device, stream):
         stream.synchronize()
         t = timed(step, steps, stream)
     total = sum(gemv_bytes(1, c['n'], c['k'], c['fmt'], c['g']) for c in cells) * steps
+    del modules
     return {'value': round(total / t / 1e9, 1), 'unit': 'GB/s', 'h2d_bytes_per_step': total_k * 2,
-            'd2h_bytes_per_step': total_n * 2, 'ms_per_step': round(t / steps * 1e3, 4)}
+            'd2h_bytes_per_step': total_n * 2, 'ms_per_step': round(t / steps * 1e3, 4),
+            'api': 'QuantizedLinear.forward per cell (fp16 activations copied in, outputs copied out every step)'}
+
+
+def gemm_flops(m, n, k, rank=RANK):
+    return 2 * m * n * k + 2 * m * rank * (n + k)
+
+
+def sweep_m_block(cells, device, stream, peak_gbs, peak_tf, ms=(16, 128, 2048), steps=10):
+    """configs[1] at its other batch sizes: every legal cell with rank-32 correction at
+    M = 16 (batched decode GEMV), 128 and 2048 (tcgen05 GEMM), each step a replayed graph
+    over all 14 cells on one of the 4 weight replicas.  Per M: GB/s and TFLOP/s of the
+    algorithmic bytes / FLOPs, and the fraction of the bound that applies (HBM while the
+    step's FLOP per byte is below the measured ridge, tensor above it)."""
+    import lowbit_runtime as rt
+    out = {}
+    gen = torch.Generator(device='cpu').manual_seed(5)
+    for m in ms:
+        xs = [torch.randn(m, c['k'], generator=gen).half().to(device) for c in cells]
+        ys = [torch.empty(m, c['n'], dtype=torch.float16, device=device) for c in cells]
+        graphs = []
+        with torch.cuda.stream(stream):
+            for c, x, y in zip(cells, xs, ys):
+                for codes, scales in c['reps']:
+                    rt.linear(x, c['fmt'], c['g'], c['n'], codes, scales, down=c['v'], up=c['u'], out=y)
+            stream.synchronize()
+            for r in range(REPLICAS):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for c, x, y in zip(cells, xs, ys):
+                        codes, scales = c['reps'][r]
+                        rt.linear(x, c['fmt'], c['g'], c['n'], codes, scales, down=c['v'], up=c['u'], out=y)
+                graphs.append(g)
+            for i in range(3):
+                graphs[i % REPLICAS].replay()
+            stream.synchronize()
+            t = timed(lambda i: graphs[i % REPLICAS].replay(), steps, stream) / steps
+        nbytes = sum(gemv_bytes(m, c['n'], c['k'], c['fmt'], c['g']) for c in cells)
+        flops = sum(gemm_flops(m, c['n'], c['k']) for c in cells)
+        gbs, tfs = nbytes / t / 1e9, flops / t / 1e12
+        bound = 'hbm' if flops / nbytes < peak_tf * 1e12 / (peak_gbs * 1e9) else 'tensor'
+        paths = sorted({rt.linear_select(c['fmt'], c['g'], m, c['n'], c['k'], RANK) for c in cells})
+        out[f'm{m}'] = {'ms_per_step': round(t * 1e3, 4), 'GB_per_s': round(gbs, 1), 'TFLOP_per_s': round(tfs, 1),
+                        'bound': bound, 'frac': round(gbs / peak_gbs if bound == 'hbm' else tfs / peak_tf, 4),
+                        'bytes_per_step': nbytes, 'flops_per_step': flops, 'paths': paths}
+        del graphs, xs, ys
+    return out
 
 
 # ---- SmolLM decode (BASELINE configs[2..4]) ----------------------------------------------
@@ -337,13 +507,14 @@ def int4_groups(config):
     return {n: (128 if s[1] % 128 == 0 else 64) for n, s in sm.SmolConfig.from_dict(config).shapes().items() if len(s) == 2}
 
 
-def build_smollm(name, mode, group, device, max_positions, rank=0, world=1, pg=None, seed=0):
+def build_smollm(name, mode, group, device, max_positions, rank=0, world=1, pg=None, seed=0, layers=None):
     """Random-init SmolLM of the named architecture (std 0.02), rank-32 corrections on every
-    projection, quantized on the GPU; tensor-parallel when world > 1 and pg is given."""
+    projection, quantized on the GPU; tensor-parallel when world > 1 and pg is given.
+    ``layers`` overrides the layer count (the dimensions stay the architecture's)."""
     import smollm_parallel as sp
     import torch_npu_smollm as sm
     from torch_npu_lowbit_correction import LowRankCorrection
-    config = SMOL[name]
+    config = SMOL[name] if layers is None else dict(SMOL[name], num_hidden_layers=layers)
     layers_w, emb, norm = sm.random_smollm_weights(config, seed=seed, device=device)
     shapes = sm.SmolConfig.from_dict(config).shapes()
     gen = torch.Generator(device=device).manual_seed(seed + 1)
@@ -356,6 +527,78 @@ def build_smollm(name, mode, group, device, max_positions, rank=0, world=1, pg=N
     layers = [sm.FrozenSmolLayer(config, w, mode=mode, group_size=group, corrections=c, device=device,
                                  max_positions=max_positions) for w, c in zip(layers_w, corrections)]
     return sm.SmolForCausalLM(sm.FrozenSmolStack(layers), emb, norm)
+
+
+def projection_formats(name, mode, group):
+    """(format, group) of each of the 7 projections for a decode entry."""
+    import torch_npu_smollm as sm
+    fmt = sm._WEIGHT_FORMATS[mode]
+    shapes = sm.SmolConfig.from_dict(SMOL[name]).shapes()
+    out = {}
+    for pname, sh in shapes.items():
+        if len(sh) != 2:
+            continue
+        g = sh[1] if fmt == 'int8' else (group.get(pname) if isinstance(group, dict) else group)
+        out[pname] = (sh, fmt, g)
+    return out
+
+
+def decode_step_bytes(name, mode, group, batch, positions, world=1, tp=False):
+    """Algorithmic HBM bytes of one decode step of the whole job: per layer the 7
+    projections' bytes_gemv (codes, scales, rank-32 factors, activations in and out), the
+    KV cache read over ``positions`` attended positions (K and V, fp16), and the tied fp16
+    LM head (2 vocab d + 2 B vocab).  Batch sharding: every rank reads the whole weights
+    for its own sequences.  Tensor parallel: weights and KV are split, the LM head is read
+    by every rank."""
+    cfg = SMOL[name]
+    layers, d, vocab = cfg['num_hidden_layers'], cfg['hidden_size'], cfg['vocab_size']
+    kvh, hd = cfg['num_key_value_heads'], 64
+
+    def one(b):
+        proj = sum(gemv_bytes(b, sh[0], sh[1], fmt, g) for sh, fmt, g in projection_formats(name, mode, group).values())
+        kv = 2 * 2 * kvh * hd * positions * b
+        return layers * (proj + kv)
+
+    head = 2 * vocab * d + 2 * batch * vocab
+    if tp:
+        return one(batch) + world * head
+    import smollm_parallel as sp
+    per = [b1 - b0 for b0, b1 in (sp.batch_shard(batch, r, world) for r in range(world))]
+    return sum(one(b) + 2 * vocab * d + 2 * b * vocab for b in per)
+
+
+def graph_kernel_nodes(graph):
+    """Kernel nodes of a captured CUDA graph (cuda-python), or None when unavailable."""
+    try:
+        from cuda.bindings import runtime as cr
+        g = cr.cudaGraph_t(init_value=graph.raw_cuda_graph())
+        err, _, count = cr.cudaGraphGetNodes(g, 0)
+        err, nodes, count = cr.cudaGraphGetNodes(g, count)
+        kernels = 0
+        for node in nodes:
+            err, kind = cr.cudaGraphNodeGetType(node)
+            if kind == cr.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                kernels += 1
+        return kernels
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def decode_entry(model, name, mode, group, batch, local_batch, prompt, steps, world, tp, pre, dec, peak_gbs, extra):
+    """One decode line: tokens/s of the whole job (``batch`` sequences), algorithmic bytes
+    per step, their rate and fraction of the HBM roofline of all GPUs, and the kernel
+    launches of this rank's captured step graph (``local_batch`` sequences)."""
+    positions = prompt + (steps + 1) / 2          # mean attended positions over the timed steps
+    nbytes = decode_step_bytes(name, mode, group, batch, positions, world, tp)
+    st = model.session(local_batch)
+    launches = graph_kernel_nodes(st['graph']) if st.get('graph') is not None else None
+    out = {'tokens_per_s': round(batch * steps / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
+           'ms_per_step': round(dec / steps * 1e3, 4), 'bytes_per_step': int(nbytes),
+           'GB_per_s': round(nbytes * steps / dec / 1e9, 1),
+           'frac_of_hbm': round(nbytes * steps / dec / 1e9 / (world * peak_gbs), 4),
+           'launches_per_step': launches}
+    out.update(extra)
+    return out
 
 
 def decode_run(model, batch, prompt, steps, world, seed=0):
@@ -380,17 +623,43 @@ def decode_run(model, batch, prompt, steps, world, seed=0):
     return pre, dec
 
 
-def decode_block(world, rank, device, pg, quick=False):
+def tp_parity_block(world, rank, device, pg, layers=2, batch=2, prompt=16, steps=16):
+    """Tensor-parallel correctness on this run's GPUs: configs[4] layer dimensions (2048,
+    32/32 heads, FFN 8192, NF4 g64, rank-32 corrections) with ``layers`` layers, greedy
+    generation tensor-parallel over all ranks vs the same model on rank 0's GPU alone."""
+    ids = torch.randint(0, SMOL['1.7b']['vocab_size'], (batch, prompt),
+                        generator=torch.Generator().manual_seed(3)).to(device)
+    tp = build_smollm('1.7b', 'nf4a16', 64, device, prompt + steps + 8, rank=rank, world=world, pg=pg, seed=7,
+                      layers=layers)
+    tokens, logits = tp.generate(ids, steps, return_logits=True)
+    result = None
+    if rank == 0:
+        single = build_smollm('1.7b', 'nf4a16', 64, device, prompt + steps + 8, seed=7, layers=layers)
+        t1, l1 = single.generate(ids, steps, return_logits=True)
+        err = max(float((a.float() - b.float()).norm() / b.float().norm()) for a, b in zip(logits, l1))
+        result = {'rel_l2': round(err, 6), 'same_tokens': bool(torch.equal(tokens, t1)), 'layers': layers,
+                  'batch': batch, 'prompt': prompt, 'steps': steps,
+                  'config': f'configs[4] dims, NF4 g64 + rank-32, tensor-parallel x{world} vs 1 GPU'}
+        del single
+    del tp
+    barrier(world)
+    torch.cuda.empty_cache()
+    return result
+
+
+def decode_block(world, rank, device, pg, peak_gbs, quick=False):
     """Decode tokens/s for BASELINE configs 2 (135M W8, B=1, rank 0 only), 3 (360M INT4 /
-    NF4, B=64 sharded over ranks, no collective) and 4 (1.7B NF4, B=32, tensor-parallel)."""
+    NF4, B=64 sharded over ranks, no collective) and 4 (1.7B NF4, B=32, tensor-parallel),
+    each with its algorithmic bytes per step and the fraction of the HBM roofline."""
     import smollm_parallel as sp
     out = {}
     if rank == 0:
         m = build_smollm('135m', 'w8a16', None, device, 128 + 128 + 8)
         pre, dec = decode_run(m, 1, 128, 128, 1)
-        out['smollm135m_w8_b1'] = {'tokens_per_s': round(128 / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
-                                   'config': 'configs[2]: 30 layers, W8 + rank-32 on all 7 projections, prompt 128, '
-                                             '128 greedy steps, batch 1, 1 GPU'}
+        out['smollm135m_w8_b1'] = decode_entry(
+            m, '135m', 'w8a16', None, 1, 1, 128, 128, 1, False, pre, dec, peak_gbs,
+            {'config': 'configs[2]: 30 layers, W8 + rank-32 on all 7 projections, prompt 128, 128 greedy steps, '
+                       'batch 1, 1 GPU'})
         del m
     barrier(world)
     b0, b1 = sp.batch_shard(64, rank, world)
@@ -398,21 +667,25 @@ def decode_block(world, rank, device, pg, quick=False):
     for tag, mode, group in (('int4', 'w4a16', int4_groups(SMOL['360m'])), ('nf4g64', 'nf4a16', 64)):
         m = build_smollm('360m', mode, group, device, 512 + steps + 8, seed=0)
         pre, dec = decode_run(m, b1 - b0, 512, steps, world, seed=rank)
-        out[f'smollm360m_{tag}_b64'] = {'tokens_per_s': round(64 * steps / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
-                                        'config': f'configs[3]: 32 layers, {tag} + rank-32, batch 64 sharded over '
-                                                  f'{world} GPU(s), prompt 512, {steps} greedy steps'}
+        out[f'smollm360m_{tag}_b64'] = decode_entry(
+            m, '360m', mode, group, 64, b1 - b0, 512, steps, world, False, pre, dec, peak_gbs,
+            {'config': f'configs[3]: 32 layers, {tag} + rank-32, batch 64 sharded over {world} GPU(s), prompt 512, '
+                       f'{steps} greedy steps'})
         del m
     torch.cuda.empty_cache()
     steps = 32 if quick else 128
     m = build_smollm('1.7b', 'nf4a16', 64, device, 2048 + steps + 8, rank=rank, world=world, pg=pg)
     pre, dec = decode_run(m, 32, 2048, steps, world)
     prefill_tokens = 32 * 2048
-    out['smollm1.7b_nf4g64_b32'] = {'tokens_per_s': round(32 * steps / dec, 1), 'prefill_ms': round(pre * 1e3, 3),
-                                    'prefill_tokens_per_s': round(prefill_tokens / pre, 1),
-                                    'config': f'configs[4]: 24 layers, NF4 g64 + rank-32, prefill 32x2048, {steps} '
-                                              f'greedy steps, {"tensor-parallel x" + str(world) if world > 1 else "1 GPU"}'}
+    out['smollm1.7b_nf4g64_b32'] = decode_entry(
+        m, '1.7b', 'nf4a16', 64, 32, 32, 2048, steps, world, True, pre, dec, peak_gbs,
+        {'prefill_tokens_per_s': round(prefill_tokens / pre, 1),
+         'config': f'configs[4]: 24 layers, NF4 g64 + rank-32, prefill 32x2048, {steps} greedy steps, '
+                   f'{"tensor-parallel x" + str(world) if world > 1 else "1 GPU"}'})
     del m
     torch.cuda.empty_cache()
+    if world > 1:
+        out['tp_parity'] = tp_parity_block(world, rank, device, pg)
     return out
 
 
@@ -490,8 +763,8 @@ def run_reference(args):
 
 
 def profile_case(which):
-    """Small, self-contained workloads for ncu captures (committed so that the profile
-    commands in profiles/ run committed files only).  dominant: the NF4 g64 8192x2048
+    """Small, self-contained workloads for ncu captures (committed, so that a capture
+    runs committed files only).  dominant: the NF4 g64 8192x2048
     decode GEMV (M=1) over 16 weight replicas (144 MB, larger than L2), 48 launches;
     prefill: the same layer at M=2048 with the rank-32 correction on the tensor-core
     path, 6 launches."""
@@ -567,8 +840,12 @@ def main():
     e2e['value'] = round(world / e2e_v, 1) if world > 1 else e2e['value']
     roof = dominant_kernel_roofline(device, stream, peak_gbs)
     roof['peak_kind'] = f'{peak_kind} HBM copy bandwidth (burst)'
-    pre_roof = prefill_roofline(device, stream, peak_tf)
-    pre_roof['peak_kind'] = f'{peak_kind} bf16 dense GEMM (burst)'
+    sweep_m = sweep_m_block(cells, device, stream, peak_gbs, peak_tf)
+    pre_roofs = {}
+    for m in PREFILL_MS:
+        pre_roofs[f'm{m}'] = prefill_roofline(device, stream, peak_tf, m)
+        pre_roofs[f'm{m}']['peak_kind'] = f'{peak_kind} bf16 dense GEMM (burst)'
+        torch.cuda.empty_cache()
     del graphs, cells
     torch.cuda.empty_cache()
     decode = None
@@ -578,7 +855,7 @@ def main():
             import torch.distributed as dist
             pg = dist.group.WORLD
         try:
-            decode = decode_block(world, rank, device, pg, quick=args.quick_decode)
+            decode = decode_block(world, rank, device, pg, peak_gbs, quick=args.quick_decode)
         except Exception as exc:  # noqa: BLE001  (report, keep the GEMV line)
             decode = {'error': f'{type(exc).__name__}: {exc}'[:300]}
     if rank != 0:
@@ -592,7 +869,7 @@ def main():
             'vs_baseline': None, 'dtype': 'u8 codes, fp16 io, fp32 accumulate', 'data': 'synthetic (seeded, BASELINE shapes)',
             'config': config_block(world),
             'frac_of_hbm_peak': round(value / world / peak_gbs, 4),
-            'e2e': e2e, 'roofline': roof, 'prefill_roofline': pre_roof, 'clocks': clocks.summary(),
+            'e2e': e2e, 'roofline': roof, 'prefill_roofline': pre_roofs, 'sweep_m': sweep_m, 'clocks': clocks.summary(),
             'gpu_launches': launches_per_step_count * args.steps}
     if decode is not None:
         line['decode'] = decode

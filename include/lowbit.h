@@ -58,8 +58,21 @@ int lb_last_cuda_error(void);
  * as the way failure handling is exercised.) */
 int lb_inject_fault(const char *entry, int count);
 /* SYNCHRONOUS: read the device-side status word at the start of a linear workspace
- * (LB_OK, or LB_ERR_TIMEOUT if a bounded wait in a tensor-core kernel gave up). */
+ * (LB_OK, or LB_ERR_TIMEOUT if a bounded device-side wait of a kernel that used it gave
+ * up: the tensor-core GEMM's pipeline waits, or the decode GEMV's wait for the correction
+ * projection computed inside the same launch).  No reference counterpart: the reference's
+ * submissions are synchronous and report driver errors per call (backend.cpp:287-293). */
 int lb_workspace_status(const void *workspace, void *stream);
+/* SYNCHRONOUS: lb_workspace_status, and when the word is set, zero the workspace header
+ * (status word and arrival counters; arrivals may have landed after a counter was reset)
+ * so that the next call starts clean.  Returns the status read. */
+int lb_workspace_check(void *workspace, size_t workspace_bytes, void *stream);
+/* Test hook, no reference counterpart: the decode GEMV's wait for its in-launch
+ * correction projection gives up after `wait_cycles` SM clock cycles (<= 0: the default,
+ * about 2 s) and, with `missing_arrivals` > 0, waits for that many arrivals more than any
+ * launch makes, so that the wait runs out.  The kernel then records LB_ERR_TIMEOUT and
+ * returns; nothing faults.  Process-wide; call with (0, 0) to restore. */
+int lb_test_wait_override(long long wait_cycles, int missing_arrivals);
 
 /*
  * Quantize + pack on the GPU.  Replaces quantize_weight (torch_npu_lowbit.py:78-105):
@@ -141,12 +154,19 @@ int lb_linear_stacked(int fmt, int group, int m, int n, int k, const uint16_t *x
  *     LB_ERR_UNSUPPORTED (use lb_linear with a workspace).
  *   - All calls on a device share the array: calls that can overlap on the GPU (for
  *     example on two streams without ordering between them) race and must not be made.
+ *   - Each call clears the array's arrival counters and status word first; read the
+ *     status with lb_noalloc_status.  An output overlapping an input is LB_ERR_ALIAS.
  */
 #define LB_NOALLOC_SCRATCH_BYTES (4u << 20)
 int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, const uint16_t *x,
                            const uint8_t *codes, const uint16_t *scales, const uint16_t *down,
                            const uint16_t *up, int rank, const uint16_t *bias, uint16_t *y,
                            void *stream);
+/* SYNCHRONOUS: the status word the last lb_linear_gemv_noalloc call on the current
+ * device left in the fixed array -- LB_OK, or LB_ERR_TIMEOUT when its bounded wait for
+ * the correction projection gave up (its y is then not valid).  A set word is cleared
+ * with the array's arrival counters.  Like lb_linear_gemv_noalloc, it allocates nothing. */
+int lb_noalloc_status(void *stream);
 
 /*
  * SmolLM decoder ops around the projections (torch_npu_smollm.py:142-193 staging,

@@ -56,11 +56,15 @@ def rope_tables(dims, positions):
 class LayerRef:
     """One decoder layer; ``packed[name]`` = (shape, fmt, group, data, scales) or None for fp16."""
 
-    def __init__(self, dims, weights, packed=None, corrections=None):
+    def __init__(self, dims, weights, packed=None, corrections=None, cache_weights=False):
+        """``cache_weights`` dequantizes each projection once and reuses it (the same
+        values; torch_npu_lowbit_demo.py:65-71), instead of per call as reference_cpu does."""
         self.dims = dims
         self.weights = {k: v.detach().half() for k, v in weights.items()}
         self.packed = packed or {}
         self.corrections = corrections or {}
+        self.cache_weights = cache_weights
+        self._prepared = {}
 
     def linear(self, v, name):
         """torch_npu_smollm.py:150-165."""
@@ -71,11 +75,17 @@ class LayerRef:
             if corr is not None:
                 value = (value + lowbit_ref.correction_delta(v, *corr)).half()
             return value
-        shape, fmt, group, data, scales = q
+        shape = q[0]
         lead = v.shape[:-1]
         flat = v.reshape(-1, v.shape[-1])
         down, up = corr if corr is not None else (None, None)
-        out = lowbit_ref.linear(flat, shape, fmt, group, data, scales, down=down, up=up)
+        if self.cache_weights:
+            w = self._prepared.get(name)
+            if w is None:
+                w = self._prepared[name] = lowbit_ref.prepare_weight(*q)
+            out = lowbit_ref.linear_prepared(flat, w, down=down, up=up)
+        else:
+            out = lowbit_ref.linear(flat, *q, down=down, up=up)
         return out.reshape(*lead, shape[0])
 
     def norm(self, v, name):

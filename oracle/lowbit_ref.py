@@ -122,6 +122,38 @@ def quantize(weight, fmt, group_size=None):
     return size, data, scale.tobytes()
 
 
+def prepare_weight(shape, fmt, group_size, data, scales):
+    """The weight operand of the per-format staging below, computed once.
+
+    * int8 with per-row scales: ``codes * scales`` in float64 (torch_npu_smollm.py:153-157).
+    * every other format: ``float32(dequantize())`` (torch_npu_smollm.py:158-159).
+    Caching it is the reference's own demo path (torch_npu_lowbit_demo.py:65-71: the
+    dequantized weight is computed once and reused); the values are the same as
+    dequantizing on every call.
+    """
+    n, k = shape
+    if fmt == 'int8' and group_size == k:
+        codes = np.frombuffer(data, dtype=np.int8).reshape(shape)
+        s = np.frombuffer(scales, dtype=np.float16).astype(np.float64)
+        return torch.from_numpy(codes.astype(np.float64) * s[:, None])
+    return torch.from_numpy(dequantize(shape, fmt, group_size, data, scales).copy()).float()
+
+
+def linear_prepared(x, weight, *, down=None, up=None, bias=None):
+    """torch_npu_smollm.py:150-164 with the weight operand from ``prepare_weight``."""
+    x = x.detach().half()
+    if weight.dtype == torch.float64:
+        value = (x.double() @ weight.t()).half()
+    else:
+        value = F.linear(x.float(), weight).half()
+    if bias is not None:
+        value = (value + bias.half()).half()
+    if down is not None:
+        delta = F.linear(F.linear(x.float(), down.float()).half().float(), up.float()).half()
+        value = (value + delta).half()
+    return value
+
+
 def linear(x, shape, fmt, group_size, data, scales, *, down=None, up=None, bias=None):
     """Per-format CPU linear staging, torch_npu_smollm.py:150-164 (plus a bias add).
 
@@ -131,23 +163,9 @@ def linear(x, shape, fmt, group_size, data, scales, *, down=None, up=None, bias=
     * correction (:160-163): ``delta = half(F.linear(half(F.linear(x, V)), U))``; ``y = half(y + delta)``.
 
     ``x`` is a CPU fp16 tensor [M, K]; ``down`` = V [r, K] and ``up`` = U [N, r] fp16 tensors.
+    The weight is dequantized on every call, as ``reference_cpu`` does (:159).
     """
-    n, k = shape
-    x = x.detach().half()
-    if fmt == 'int8' and group_size == k:
-        codes = np.frombuffer(data, dtype=np.int8).reshape(shape)
-        s = np.frombuffer(scales, dtype=np.float16).astype(np.float64)
-        weight = torch.from_numpy(codes.astype(np.float64) * s[:, None])
-        value = (x.double() @ weight.t()).half()
-    else:
-        w = torch.from_numpy(dequantize(shape, fmt, group_size, data, scales).copy())
-        value = F.linear(x.float(), w.float()).half()
-    if bias is not None:
-        value = (value + bias.half()).half()
-    if down is not None:
-        delta = F.linear(F.linear(x.float(), down.float()).half().float(), up.float()).half()
-        value = (value + delta).half()
-    return value
+    return linear_prepared(x, prepare_weight(shape, fmt, group_size, data, scales), down=down, up=up, bias=bias)
 
 
 def correction_delta(x, down, up):

@@ -20,7 +20,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get('REF', '/root/reference'))
+if not os.environ.get('REF'):
+    sys.exit('set REF to the reference checkout (the directory holding torch_npu_lowbit.py)')
+REF = Path(os.environ['REF'])
 sys.path[:0] = [str(REF), str(REF / 'npunlock/python')]
 
 import torch_npu_lowbit as lb  # noqa: E402

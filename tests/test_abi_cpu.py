@@ -127,3 +127,27 @@ def test_host_fault_injection(lib):
     assert lib.lb_rmsnorm(P(16), None, None, P(16), P(4096), 1, 8, 1e-5, None) == 8
     with pytest.raises(RuntimeError, match='injected'):
         rt.check(8, 'lb_linear')
+
+
+def test_noalloc_entry_validates_and_injects_before_any_launch(lib):
+    """The allocation-free GEMV takes the same host-side failure paths as lb_linear: the
+    injection hook, argument checks and the alias check, all before touching CUDA."""
+    import lowbit_runtime as rt
+    P = ctypes.c_void_p
+    f = lib.lb_linear_gemv_noalloc
+    rt.inject_fault('lb_linear_gemv_noalloc', 1)
+    assert f(1, 64, 1, 64, 128, P(16), P(4096), P(8192), None, None, 0, None, P(1 << 20), None) == rt.INJECTED
+    assert f(9, 64, 1, 64, 128, P(16), P(4096), P(8192), None, None, 0, None, P(1 << 20), None) == rt.INVALID
+    assert f(1, 64, 1, 64, 128, P(16), P(4096), P(8192), P(16), None, 32, None, P(1 << 20), None) == rt.INVALID
+    assert f(1, 64, 65, 64, 128, P(16), P(4096), P(8192), None, None, 0, None, P(1 << 20), None) == rt.UNSUPPORTED
+    # y overlapping x / the codes / the correction factors
+    assert f(1, 64, 1, 64, 128, P(1 << 20), P(4096), P(8192), None, None, 0, None, P(1 << 20), None) == rt.ALIAS
+    assert f(1, 64, 1, 64, 128, P(16), P(1 << 20), P(8192), None, None, 0, None, P(1 << 20), None) == rt.ALIAS
+    assert f(1, 64, 1, 64, 128, P(16), P(4096), P(8192), P(1 << 20), P(1 << 16), 32, None, P(1 << 20), None) == rt.ALIAS
+
+
+def test_timeout_status_maps_to_its_own_error():
+    import lowbit_runtime as rt
+    with pytest.raises(rt.LowbitTimeoutError, match='timed out'):
+        rt.check(rt.TIMEOUT, 'lb_linear')
+    assert issubclass(rt.LowbitTimeoutError, RuntimeError)

@@ -283,3 +283,59 @@ def test_stacked_linear_matches_separate_projections(rt, fmt, g, m):
     assert torch.equal(y2.cpu(), (y.float().cpu() + resid.float()).half())
     with pytest.raises(ValueError):
         rt.linear_stacked(torch.zeros(65, k, dtype=torch.float16, device='cuda'), fmt, group, ntot, codes, scales)
+
+
+# ---- BASELINE configs[0] and configs[1] at their own sizes --------------------------------
+SWEEP_SHAPES = [(1536, 576), (576, 1536), (8192, 2048), (2048, 8192)]
+SWEEP_CELLS = [(fmt, g, n, k) for (n, k) in SWEEP_SHAPES for fmt in ('int4', 'nf4') for g in (64, 128) if k % g == 0]
+_SWEEP_CACHE = {}
+
+
+def _sweep_cell(n, k, fmt, g):
+    """Seed-0 weight and factors of the shape, quantized by the oracle once
+    per module; group 128 with K=576 is not representable and is not a cell."""
+    key = (n, k, fmt, g)
+    if key not in _SWEEP_CACHE:
+        w, u, v = baseline_weight(n, k, seed=0)
+        group, data, scales = ref.quantize(w.numpy(), fmt, g)
+        prepared = ref.prepare_weight((n, k), fmt, group, data, scales)
+        _SWEEP_CACHE.clear()   # one cell at a time: the big shapes' prepared weights are 64 MB
+        _SWEEP_CACHE[key] = (group, data, scales, prepared, u, v)
+    return _SWEEP_CACHE[key]
+
+
+def test_sweep_has_fourteen_legal_cells():
+    assert len(SWEEP_CELLS) == 14
+    assert ('int4', 128, 1536, 576) not in SWEEP_CELLS and ('nf4', 128, 1536, 576) not in SWEEP_CELLS
+
+
+@pytest.mark.parametrize('m', [16, 128, 2048])
+@pytest.mark.parametrize('fmt,g,n,k', SWEEP_CELLS)
+def test_sweep_cell_matches_oracle_at_full_batch(rt, fmt, g, n, k, m):
+    """Every legal configs[1] cell at M = 16, 128 and 2048, every output row against the
+    oracle (rank-32 correction included): the batched-decode GEMV and the tcgen05 GEMM at
+    the sweep's own sizes."""
+    group, data, scales, prepared, u, v = _sweep_cell(n, k, fmt, g)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(1000 + m)).half()
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    expected = ref.linear_prepared(x, prepared, down=v, up=u)
+    y = rt.linear(x.cuda(), fmt, group, n, codes, sc, down=v.cuda(), up=u.cuda())
+    _compare(y, expected, (fmt, g, n, k, m, rt.linear_select(fmt, group, m, n, k, 32)))
+
+
+@pytest.mark.parametrize('m', [1, 128])
+def test_config0_w8_linear_matches_oracle(rt, m):
+    """W (1536, 576) ~ N(0, 0.02^2) from seed 0, per-channel symmetric int8,
+    U [1536, 32] and V [32, 576] ~ N(0, 1e-3^2) drawn after W from the same generator,
+    X ~ N(0, 1) of shape [1, 576] (decode) and [128, 576] (prefill)."""
+    n, k = 1536, 576
+    w, u, v = baseline_weight(n, k, seed=0)
+    group, data, scales = ref.quantize(w.numpy(), 'int8')
+    assert group == k
+    codes, sc = rt.quantize_pack(w.cuda(), 'int8', k)
+    assert codes.cpu().numpy().tobytes() == data and sc.cpu().numpy().tobytes() == scales
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(2000 + m)).half()
+    expected = _oracle(x, (n, k), 'int8', group, data, scales, down=v, up=u)
+    y = rt.linear(x.cuda(), 'int8', group, n, codes, sc, down=v.cuda(), up=u.cuda())
+    _compare(y, expected, ('config0', m, rt.linear_select('int8', group, m, n, k, 32)))

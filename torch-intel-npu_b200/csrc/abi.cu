@@ -30,6 +30,7 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
                                 const uint16_t *bias, uint16_t *y, void *scratch, int *counters, float *zpart,
                                 int *err, cudaStream_t st, bool *fused);
 size_t gemv_fused_zpart_bytes(int m);
+void set_wait_override(long long cycles, int missing);
 cudaError_t launch_linear_generic(int fmt, int group, int m, int n, int k, const uint16_t *x, const uint8_t *codes,
                                   const uint16_t *scales, const uint16_t *z, const uint16_t *up, int rank,
                                   const uint16_t *bias, uint16_t *y, cudaStream_t st);
@@ -77,14 +78,14 @@ bool pdl_enabled() {
 
 using namespace lowbit_host;
 
+namespace lowbit_host {
 namespace {
-thread_local int g_last_cuda_error = 0;
-
 // Host-side fault injection: the next `count` calls of entry `name` fail with
 // LB_ERR_INJECTED before launching anything (no device fault is ever produced).
 std::mutex g_inject_mu;
 std::string g_inject_name;
 std::atomic<int> g_inject_count{0};
+}  // namespace
 
 bool injected(const char *entry) {
   if (g_inject_count.load(std::memory_order_relaxed) <= 0) return false;
@@ -95,6 +96,34 @@ bool injected(const char *entry) {
   return true;
 }
 
+bool overlaps(const void *a, size_t na, const void *b, size_t nb) {
+  if (!a || !b || !na || !nb) return false;
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + nb && y < x + na;
+}
+
+size_t code_bytes(int fmt, int64_t n, int64_t k) {
+  const int64_t c = n * k;
+  if (fmt == LB_FMT_INT8) return size_t(c);
+  if (fmt == LB_FMT_FP16) return size_t(c) * 2;
+  return size_t((c + 1) / 2);
+}
+
+int linear_alias_status(int fmt, int group, int m, int n, int k, const void *x, const void *codes, const void *scales,
+                        const void *down, const void *up, int rank, const void *bias, const void *y) {
+  const size_t yb = size_t(m) * n * 2;
+  if (overlaps(y, yb, x, size_t(m) * k * 2) || overlaps(y, yb, codes, code_bytes(fmt, n, k)) ||
+      (scales && overlaps(y, yb, scales, size_t(n) * (k / group) * 2)) ||
+      (bias && overlaps(y, yb, bias, size_t(n) * 2)) || (down && overlaps(y, yb, down, size_t(rank) * k * 2)) ||
+      (up && overlaps(y, yb, up, size_t(n) * rank * 2)))
+    return LB_ERR_ALIAS;
+  return LB_OK;
+}
+}  // namespace lowbit_host
+
+namespace {
+thread_local int g_last_cuda_error = 0;
+
 int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return LB_OK;
   g_last_cuda_error = int(e);
@@ -103,20 +132,7 @@ int cuda_status(cudaError_t e) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-bool overlaps(const void *a, size_t na, const void *b, size_t nb) {
-  if (!a || !b || !na || !nb) return false;
-  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
-  return x < y + nb && y < x + na;
-}
-
 bool valid_format(int fmt) { return fmt == LB_FMT_INT4 || fmt == LB_FMT_NF4 || fmt == LB_FMT_INT8 || fmt == LB_FMT_FP16; }
-
-size_t code_bytes(int fmt, int64_t n, int64_t k) {
-  const int64_t c = n * k;
-  if (fmt == LB_FMT_INT8) return size_t(c);
-  if (fmt == LB_FMT_FP16) return size_t(c) * 2;
-  return size_t((c + 1) / 2);
-}
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -275,11 +291,8 @@ int lb_linear_path(int path, int fmt, int group, int m, int n, int k, const uint
   if (path != LB_PATH_GEMV && path != LB_PATH_TC && path != LB_PATH_GENERIC) return LB_ERR_INVALID_ARGUMENT;
   const size_t need = linear_ws(path, fmt, group, m, n, k, rank);
   if (!workspace || workspace_bytes < need) return LB_ERR_WORKSPACE;
-  const size_t yb = size_t(m) * n * 2;
-  if (overlaps(y, yb, x, size_t(m) * k * 2) || overlaps(y, yb, codes, code_bytes(fmt, n, k)) ||
-      (scales && overlaps(y, yb, scales, size_t(n) * (k / group) * 2)) ||
-      (bias && overlaps(y, yb, bias, size_t(n) * 2)) || (down && overlaps(y, yb, down, size_t(rank) * k * 2)) ||
-      (up && overlaps(y, yb, up, size_t(n) * rank * 2)) || overlaps(y, yb, workspace, need))
+  if (linear_alias_status(fmt, group, m, n, k, x, codes, scales, down, up, rank, bias, y) != LB_OK ||
+      overlaps(y, size_t(m) * n * 2, workspace, need))
     return LB_ERR_ALIAS;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -377,6 +390,24 @@ int lb_workspace_status(const void *workspace, void *stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e);
   return flag;
+}
+
+int lb_workspace_check(void *workspace, size_t workspace_bytes, void *stream) {
+  if (!workspace || workspace_bytes < kHeader) return LB_ERR_INVALID_ARGUMENT;
+  const int flag = lb_workspace_status(workspace, stream);
+  if (flag == LB_OK || flag == LB_ERR_CUDA) return flag;
+  // a wait gave up: arrivals may have landed after the counters were reset, so the
+  // status word and every counter start again from zero
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, kHeader, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_status(e);
+  return flag;
+}
+
+int lb_test_wait_override(long long wait_cycles, int missing_arrivals) {
+  set_wait_override(wait_cycles, missing_arrivals);
+  return LB_OK;
 }
 
 int lb_rmsnorm(const uint16_t *x, const uint16_t *residual, uint16_t *residual_out, const uint16_t *gamma,

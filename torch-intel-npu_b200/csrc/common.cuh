@@ -172,6 +172,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // Host-side launch helpers.
 namespace lowbit_host {
+// abi.cu: host-side fault injection, pointer-range overlap and the alias checks of a
+// linear call (an output overlapping an input), shared by every linear entry point
+bool injected(const char *entry);
+bool overlaps(const void *a, size_t na, const void *b, size_t nb);
+size_t code_bytes(int fmt, int64_t n, int64_t k);
+int linear_alias_status(int fmt, int group, int m, int n, int k, const void *x, const void *codes, const void *scales,
+                        const void *down, const void *up, int rank, const void *bias, const void *y);
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) is a driver round trip: issue it once
 // per (kernel, device) and whenever a larger size is requested.

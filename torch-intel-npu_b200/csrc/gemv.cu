@@ -25,6 +25,7 @@
 // run an epilogue wait (bounded) for all slices and sum them in slice order.  The GEMV
 // of a large weight outlasts that chain, so the projection costs no launch of its own.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 
@@ -70,6 +71,8 @@ struct GemvParams {
   int zx;
   float *zpart;
   int *err;
+  long long wait_cycles;   // bound of the epilogues' wait for the slices (clock cycles)
+  int z_extra;             // test hook: arrivals waited for beyond the slices (0 in use)
 };
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
@@ -406,11 +409,11 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     if (p.zv) {
       // wait (bounded) for every K slice of z, then z = half(sum of the slices in order)
       if (threadIdx.x == 0) {
-        const int slices = p.zx * gridDim.y;
-        if (ld_acquire(p.counters + kZArrive) < slices) {
+        const int want = p.zx * gridDim.y + p.z_extra;
+        if (ld_acquire(p.counters + kZArrive) < want) {
           const long long t0 = clock64();
-          while (ld_acquire(p.counters + kZArrive) < slices)
-            if (clock64() - t0 > kWaitCycles) { atomicExch(p.err, LB_ERR_TIMEOUT); break; }
+          while (ld_acquire(p.counters + kZArrive) < want)
+            if (clock64() - t0 > p.wait_cycles) { atomicExch(p.err, LB_ERR_TIMEOUT); break; }
         }
       }
       __syncthreads();
@@ -815,6 +818,16 @@ template <int FMT> static int resident_ctas_f(int ncol) {
 constexpr int kFuseZMaxRows = 16;
 constexpr int64_t kFuseZMinBytes = int64_t(4) << 20;
 
+// Test hook (lb_test_wait_override): the fused projection's wait bound and a number of
+// arrivals that no launch makes, so that a test can make the wait run out.
+std::atomic<long long> g_wait_cycles{kWaitCycles};
+std::atomic<int> g_z_extra{0};
+
+void set_wait_override(long long cycles, int missing) {
+  g_wait_cycles.store(cycles > 0 ? cycles : kWaitCycles);
+  g_z_extra.store(missing > 0 ? missing : 0);
+}
+
 size_t gemv_fused_zpart_bytes(int m) {
   return m <= kFuseZMaxRows ? size_t(kMaxZSlices) * m * 32 * sizeof(float) : 0;
 }
@@ -947,6 +960,8 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
   p.zx = zx;
   p.zpart = zpart;
   p.err = err;
+  p.wait_cycles = g_wait_cycles.load();
+  p.z_extra = g_z_extra.load();
   p.up = reinterpret_cast<const __half *>(up);
   p.rank = rank;
   p.zs = 32;

@@ -74,6 +74,7 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
                                       const uint16_t *scales, const uint16_t *down, const uint16_t *up, int rank,
                                       const uint16_t *bias, uint16_t *y, void *stream) {
   using namespace lowbit_host;
+  if (injected("lb_linear_gemv_noalloc")) return LB_ERR_INJECTED;
   if (!(fmt == LB_FMT_INT4 || fmt == LB_FMT_NF4 || fmt == LB_FMT_INT8 || fmt == LB_FMT_FP16) || m < 1 || n < 1 ||
       k < 1 || !x || !codes || !y || (fmt != LB_FMT_FP16 && (!scales || group < 1 || group > k || k % group)))
     return LB_ERR_INVALID_ARGUMENT;
@@ -87,14 +88,17 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
   if (size_t(m) * 32 * 2 > kZBytes || gemv_fused_zpart_bytes(m) > kZBytes ||
       gemv_workspace_bytes(fmt, m, n, k) > size_t(LB_NOALLOC_SCRATCH_BYTES) - kPartialOffset)
     return LB_ERR_WORKSPACE;     // the problem needs more scratch than the fixed array holds
+  if (linear_alias_status(fmt, group, m, n, k, x, codes, scales, down, up, rank, bias, y) != LB_OK)
+    return LB_ERR_ALIAS;
   void *base = nullptr;
   cudaError_t e = scratch_address(&base);
   if (e != cudaSuccess) return LB_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *s = static_cast<uint8_t *>(base);
   int *counters = reinterpret_cast<int *>(s);
-  // The array keeps whatever the previous call left; the counters must start at zero.
-  e = cudaMemsetAsync(counters, 0, kCounterBytes, st);
+  // The array keeps whatever the previous call left; the counters and the status word
+  // (contiguous at its start) must start at zero.
+  e = cudaMemsetAsync(counters, 0, kZOffset, st);
   if (e == cudaSuccess && rank > 0) {   // the same fused projection lb_linear would run
     bool fused = false;
     e = launch_gemv_fused_z(fmt, group, m, n, k, x, codes, scales, down, up, rank, bias, y, s + kPartialOffset,
@@ -111,4 +115,24 @@ extern "C" int lb_linear_gemv_noalloc(int fmt, int group, int m, int n, int k, c
     e = launch_gemv(fmt, group, m, n, k, x, codes, scales, z, 32, up, rank, bias, nullptr, y, s + kPartialOffset,
                     counters, st);
   return e == cudaSuccess ? LB_OK : LB_ERR_CUDA;
+}
+
+// SYNCHRONOUS: waits for `stream`, then returns the status word of the current device's
+// array (LB_OK, or LB_ERR_TIMEOUT when a bounded wait of the last call on it gave up, in
+// which case its output is not valid) and clears it with the arrival counters.
+extern "C" int lb_noalloc_status(void *stream) {
+  void *base = nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = scratch_address(&base);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return LB_ERR_CUDA;
+  uint8_t *s = static_cast<uint8_t *>(base);
+  int flag = 0;
+  e = cudaMemcpyAsync(&flag, s + kStatusOffset, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && flag != LB_OK) {
+    e = cudaMemsetAsync(s, 0, kZOffset, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  return e == cudaSuccess ? flag : LB_ERR_CUDA;
 }

@@ -11,6 +11,7 @@ entry point raises.
 """
 import ctypes
 import functools
+import os
 import threading
 from pathlib import Path
 
@@ -54,11 +55,19 @@ SIGNATURES = {
     'lb_argmax': ([_P, _I, _I, _P, _P, _S, _P], _I),
     'lb_argmax_workspace_bytes': ([_I, _I], _S),
     'lb_linear_gemv_noalloc': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P], _I),
+    'lb_noalloc_status': ([_P], _I),
+    'lb_workspace_check': ([_P, _S, _P], _I),
+    'lb_test_wait_override': ([ctypes.c_longlong, _I], _I),
 }
 
 
 class LowbitCudaError(RuntimeError):
     """A CUDA launch or runtime failure reported by liblowbit (status LB_ERR_CUDA)."""
+
+
+class LowbitTimeoutError(RuntimeError):
+    """A bounded device-side wait gave up (status LB_ERR_TIMEOUT): the kernel returned
+    without faulting, but the output of the call that recorded it is not valid."""
 
 
 def load_library():
@@ -133,6 +142,8 @@ def check(status, what):
         raise ValueError(f'{what}: {text}')
     if status == CUDA_ERR:
         raise LowbitCudaError(f'{what}: {text} (cudaError {lib().lb_last_cuda_error()})')
+    if status == TIMEOUT:
+        raise LowbitTimeoutError(f'{what}: {text}')
     raise RuntimeError(f'{what}: {text}')
 
 
@@ -179,6 +190,35 @@ class Workspace:
     @classmethod
     def reserve(cls, nbytes, device=None):
         return cls.get(nbytes, device)
+
+    @classmethod
+    def check(cls, index=None):
+        """SYNCHRONOUS: read (and on a set word, reset) the status word of every workspace
+        of device ``index`` (all devices when None); raises LowbitTimeoutError if a
+        bounded device-side wait of a kernel that used one gave up."""
+        L = lib()
+        for (dev, stream), buf in list(cls._buffers.items()):
+            if index is not None and dev != index:
+                continue
+            with torch.cuda.device(dev):
+                check(L.lb_workspace_check(buf.data_ptr(), buf.numel(), stream), 'workspace status')
+
+
+def check_device_waits(device=None):
+    """Raise LowbitTimeoutError if any linear on ``device`` recorded a timed-out device
+    wait since the last check (synchronises the device's workspace streams)."""
+    Workspace.check(None if device is None else cuda_device(device).index)
+
+
+# LOWBIT_CHECK_WAITS=1: every eager ``linear`` call (not under CUDA graph capture) reads
+# its workspace status word afterwards and raises on a timed-out wait.  Synchronous, so
+# for debugging; graph replays are checked with check_device_waits().
+CHECK_WAITS = os.environ.get('LOWBIT_CHECK_WAITS', '0') == '1'
+
+
+def set_wait_checks(enabled):
+    global CHECK_WAITS
+    CHECK_WAITS = bool(enabled)
 
 
 def inject_fault(entry='*', count=1):
@@ -256,6 +296,8 @@ def linear(x, fmt, group, n, codes, scales, *, down=None, up=None, bias=None, ou
                   _addr(up), rank, _addr(bias), y.data_ptr(), ws.data_ptr(), ws.numel(), stream)
     if status != OK:
         check(status, 'lb_linear')
+    if CHECK_WAITS and not torch.cuda.is_current_stream_capturing():
+        check(L.lb_workspace_check(ws.data_ptr(), ws.numel(), stream), 'lb_linear')
     return y
 
 

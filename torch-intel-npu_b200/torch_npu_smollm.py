@@ -664,7 +664,7 @@ class SmolForCausalLM(torch.nn.Module):
             self._decode_step(st)            # warm-up: sizes workspaces outside capture
             st['lengths'].copy_(saved)
             st['ids'].copy_(ids)
-            g = torch.cuda.CUDAGraph()
+            g = torch.cuda.CUDAGraph(keep_graph=True)   # kept for launch counting (cudaGraphGetNodes)
             with torch.cuda.graph(g, stream=side):
                 st['logits'] = self._decode_step(st)
         stream.wait_stream(side)
@@ -687,6 +687,9 @@ class SmolForCausalLM(torch.nn.Module):
             tokens[:, t] = st['ids']
             if return_logits:
                 all_logits.append(out.clone())
+        # a bounded device-side wait that ran out inside a replayed step is reported here
+        # (one synchronising read of each workspace status word)
+        rt.check_device_waits(self.device)
         return (tokens, all_logits) if return_logits else tokens
 
 
