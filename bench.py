@@ -526,7 +526,7 @@ def build_smollm(name, mode, group, device, max_positions, rank=0, world=1, pg=N
                                      rank=rank, world=world, group=pg, device=device, max_positions=max_positions)
     layers = [sm.FrozenSmolLayer(config, w, mode=mode, group_size=group, corrections=c, device=device,
                                  max_positions=max_positions) for w, c in zip(layers_w, corrections)]
-    return sm.SmolForCausalLM(sm.FrozenSmolStack(layers), emb, norm)
+    return sm.SmolForCausalLM(sm.FrozenSmolStack.from_layers(layers), emb, norm)
 
 
 def projection_formats(name, mode, group):

@@ -84,7 +84,7 @@ def build(config, mode, group, corrected, seed=0):
         gpu_layers.append(sm.FrozenSmolLayer(config, w, mode=mode, packed_weights=packed, corrections=corr, max_positions=128))
         ocorr = None if corr is None else {n: c.tensors() for n, c in corr.items()}
         ref_layers.append(dref.LayerRef(dims, w, opacked, ocorr, cache_weights=True))
-    model = sm.SmolForCausalLM(sm.FrozenSmolStack(gpu_layers), emb, norm)
+    model = sm.SmolForCausalLM(sm.FrozenSmolStack.from_layers(gpu_layers), emb, norm)
     oracle = dref.DecoderRef(dims, ref_layers, emb, norm, 128)
     return model, oracle
 

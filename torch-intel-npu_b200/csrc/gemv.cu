@@ -138,8 +138,16 @@ __device__ __forceinline__ void gemv_z_slice(const GemvParams &p) {
 // Reduction buffer: [warps_k][rows_cta][LDC] floats, warps_k * rows_cta <= 128 * row groups.
 template <int NCOL> constexpr int red_words() { return 128 * (NCOL > 2 ? 1 : kMaxRowGroups) * 8 * NCOL; }
 
-template <int FMT, int NCOL>
+// GS (one activation row, 4-bit formats, group 64 or 128): the codes are decoded without
+// their scale, every m16n8k16 tile lies inside one scale group, each group's tiles start a
+// fresh fp32 partial (zero accumulator) and the group scale multiplies that partial --
+// one FFMA per group and row instead of one fp16 multiply per weight pair.  The products
+// code * x are exact in fp32, so the result differs from the reference's
+// sum(rn16(code * scale) * x) only by the fp16 rounding of each code * scale.
+template <int FMT, int NCOL, int GS = 0>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
+  static_assert(GS == 0 || (NCOL == 1 && (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) && (GS == 64 || GS == 128)),
+                "group-scaled accumulation is for one activation row of 4-bit codes, group 64 or 128");
   constexpr int E = FmtTraits<FMT>::E;
   constexpr int NP = E / 2;          // pairs per lane chunk
   constexpr int TILES = NP / 2;      // m16n8k16 tiles per K block
@@ -192,6 +200,18 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         for (int h = 0; h < 2; ++h) {
           const int row = wrow0 + 16 * r + g + 8 * h;
           const bool ok = r < p.rpw && kvalid && row < p.n;
+          if constexpr (GS == 64) {
+            // the block's two groups (lanes t = 0, 1 and t = 2, 3) and both their scales
+            q[u][r][h] = ok ? ldg_nc_v4(code_base + (16 * r + 8 * h) * row_bytes + int64_t(kb) * 64) : make_uint4(0, 0, 0, 0);
+            const uint32_t sv = ok ? *reinterpret_cast<const uint32_t *>(scale_base + (16 * r + 8 * h) * groups_per_row + 2 * kb) : 0u;
+            s2[u][r][h] = u32_as_h2(sv);
+            continue;
+          } else if constexpr (GS == 128) {
+            q[u][r][h] = ok ? ldg_nc_v4(code_base + (16 * r + 8 * h) * row_bytes + int64_t(kb) * 64) : make_uint4(0, 0, 0, 0);
+            const __half sc = ok ? scale_base[(16 * r + 8 * h) * groups_per_row + kb] : __float2half(0.f);
+            s2[u][r][h] = __halves2half2(sc, sc);
+            continue;
+          }
           q[u][r][h] = ok ? ldg_nc_v4(code_base + (16 * r + 8 * h) * row_bytes + int64_t(kb) * 64) : make_uint4(0, 0, 0, 0);
           if constexpr (FMT != LB_FMT_FP16) {
             const __half sc = (ok && !per_row_scale) ? scale_base[(16 * r + 8 * h) * groups_per_row + gi]
@@ -224,6 +244,14 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       for (int r = lane; r < rows; r += 32)
         prefetch_l2_bulk(p.codes + int64_t(row0 + r) * row_bytes + off, uint32_t(end - off));
   }
+  if (p.up && (p.z || p.zv) && warp == kWarps - 1 && lane == 0 && blockIdx.y == 0) {
+    // the correction factor rows of the CTA's epilogue (U is as constant as the codes):
+    // in L2 by the time the main loop ends
+    const int rows = min(rows_cta, p.n - row0);
+    const __half *u0 = p.up + int64_t(row0) * p.rank;
+    const uint32_t bytes = uint32_t(rows) * p.rank * 2;
+    if ((bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(u0) & 15) == 0) prefetch_l2_bulk(u0, bytes);
+  }
   if constexpr (FMT == LB_FMT_NF4) {
     fill_nf4_pair_lut<64>(lut);
     __syncthreads();
@@ -248,7 +276,53 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   // x pairs of a round, then dequant + MMA of its weights.
   auto compute_round = [&](int kbA, const uint4 (&q)[2][RG][2], const __half2 (&s2)[2][RG][2]) {
     const bool scale = kScaled4 || (FMT == LB_FMT_INT8 && !per_row_scale);
-    if constexpr (!kWide) {
+    if constexpr (GS != 0) {
+      // One activation row.  B column c holds x only at the K positions of scale group c
+      // of the block: group 128 -- lanes g == 0 supply x; group 64 -- lanes (0, t < 2) and
+      // (1, t >= 2), the lanes whose 32 elements lie in the block's first / second group.
+      // So D column c is group c's partial sum: lanes t == 0 hold columns 0 and 1 of rows
+      // g and g + 8, every other column stays zero.
+      const bool xlane = GS == 128 ? g == 0 : g == (t >> 1);
+      uint32_t xr[2][NP];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int kb = kbA + u * p.warps_k;
+        const int chunk = kb * 4 + t;
+        load_x_pairs<FMT>(p.x, chunk, kb < kb1 && chunk < chunks && xlane, xr[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && kbA + p.warps_k >= kb1) break;
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+          if (r >= p.rpw) break;
+          uint32_t a0[NP], a1[NP];
+          unpack_chunk<FMT>(q[u][r][0], s2[u][r][0], false, lutb, lane4, a0);
+          unpack_chunk<FMT>(q[u][r][1], s2[u][r][1], false, lutb, lane4, a1);
+          float d0[4], d1[4];   // two chains (even / odd tiles), each started from zero
+#pragma unroll
+          for (int j = 0; j < TILES; j += 2) {
+            const uint32_t aa[4] = {a0[2 * j], a1[2 * j], a0[2 * j + 1], a1[2 * j + 1]};
+            const uint32_t ab[4] = {a0[2 * j + 2], a1[2 * j + 2], a0[2 * j + 3], a1[2 * j + 3]};
+            if (j == 0) {
+              mma16816_zero(d0, aa, xr[u][2 * j], xr[u][2 * j + 1]);
+              mma16816_zero(d1, ab, xr[u][2 * j + 2], xr[u][2 * j + 3]);
+            } else {
+              mma16816(d0, aa, xr[u][2 * j], xr[u][2 * j + 1]);
+              mma16816(d1, ab, xr[u][2 * j + 2], xr[u][2 * j + 3]);
+            }
+          }
+          const float2 sg = __half22float2(s2[u][r][0]), sg8 = __half22float2(s2[u][r][1]);
+          if constexpr (GS == 64) {
+            acc[r][0][0][0] = fmaf(d0[1] + d1[1], sg.y, fmaf(d0[0] + d1[0], sg.x, acc[r][0][0][0]));
+            acc[r][0][0][2] = fmaf(d0[3] + d1[3], sg8.y, fmaf(d0[2] + d1[2], sg8.x, acc[r][0][0][2]));
+          } else {
+            acc[r][0][0][0] = fmaf(d0[0] + d1[0], sg.x, acc[r][0][0][0]);
+            acc[r][0][0][2] = fmaf(d0[2] + d1[2], sg8.x, acc[r][0][0][2]);
+          }
+        }
+      }
+    } else if constexpr (!kWide) {
       uint32_t xr[2][NCOL][NP];
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
@@ -435,6 +509,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     }
   }
   const int ktiles = zstride / 16;
+  // even rank and a 4-byte aligned U: factor pairs are read as one word
+  const bool u_pairs = (p.rank & 1) == 0 && (reinterpret_cast<uintptr_t>(p.up) & 3) == 0;
   for (int rg = warp; rg < rows_cta / 16; rg += kWarps) {
     const int rl0 = rg * 16;
 #pragma unroll
@@ -447,14 +523,16 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int row = row0 + rl0 + g + 8 * (i & 1);
-          const int kk = 16 * kt + 2 * t + 8 * (i >> 1);
-          __half lo = __float2half(0.f), hi = lo;
-          if (row < p.n) {
-            const __half *ur = p.up + int64_t(row) * p.rank;
-            if (kk < p.rank) lo = ur[kk];
-            if (kk + 1 < p.rank) hi = ur[kk + 1];
+          const int kk = 16 * kt + 2 * t + 8 * (i >> 1);   // even
+          const __half *ur = p.up + int64_t(row) * p.rank;
+          if (row >= p.n || kk >= p.rank) {
+            ua[i] = 0u;
+          } else if (u_pairs) {
+            ua[i] = *reinterpret_cast<const uint32_t *>(ur + kk);   // U[row][kk], U[row][kk + 1]
+          } else {
+            const __half lo = ur[kk], hi = kk + 1 < p.rank ? ur[kk + 1] : __float2half(0.f);
+            ua[i] = h2_as_u32(__halves2half2(lo, hi));
           }
-          ua[i] = h2_as_u32(__halves2half2(lo, hi));
         }
         uint32_t b0 = 0, b1 = 0;
         if (mz < p.m) {
@@ -807,9 +885,30 @@ static int resident_ctas(const void *kern, size_t smem) {
 template <int FMT, int NCOL> static size_t gemv_smem_v() {
   return size_t(red_words<NCOL>()) * sizeof(float) + (FMT == LB_FMT_NF4 ? size_t(kLutWords) * 4 : 0);
 }
-template <int FMT> static int resident_ctas_f(int ncol) {
+template <int FMT> static int resident_ctas_f(int ncol, int gs) {
+  if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
+    if (ncol == 1 && gs == 64)
+      return resident_ctas(reinterpret_cast<const void *>(gemv_kernel<FMT, 1, 64>), gemv_smem_v<FMT, 1>());
+    if (ncol == 1 && gs == 128)
+      return resident_ctas(reinterpret_cast<const void *>(gemv_kernel<FMT, 1, 128>), gemv_smem_v<FMT, 1>());
+  }
   return ncol == 1 ? resident_ctas(reinterpret_cast<const void *>(gemv_kernel<FMT, 1>), gemv_smem_v<FMT, 1>())
                    : resident_ctas(reinterpret_cast<const void *>(gemv_kernel<FMT, 2>), gemv_smem_v<FMT, 2>());
+}
+
+// Group-scaled accumulation (gemv_kernel's GS) applies to one activation row of INT4 / NF4
+// codes with group 64 (K a multiple of 128 and 4-byte aligned scales: two groups' scales
+// are read as one word) or 128.  LOWBIT_GEMV_GS=0 turns it off (comparison).
+static int gemv_gs(int fmt, int group, int m, int k, const void *scales) {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char *e = getenv("LOWBIT_GEMV_GS");
+    enabled = (e && e[0] == '0') ? 0 : 1;
+  }
+  if (!enabled || m != 1 || (fmt != LB_FMT_INT4 && fmt != LB_FMT_NF4)) return 0;
+  if (group == 64 && k % 128 == 0 && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) return 64;
+  if (group == 128) return 128;
+  return 0;
 }
 
 // Activation rows and weight bytes from which the projection is fused into the GEMV
@@ -832,9 +931,9 @@ size_t gemv_fused_zpart_bytes(int m) {
   return m <= kFuseZMaxRows ? size_t(kMaxZSlices) * m * 32 * sizeof(float) : 0;
 }
 
-template <int FMT, int NCOL>
+template <int FMT, int NCOL, int GS = 0>
 static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t, cudaStream_t st) {
-  auto kern = gemv_kernel<FMT, NCOL>;
+  auto kern = gemv_kernel<FMT, NCOL, GS>;
   size_t smem = size_t(red_words<NCOL>()) * sizeof(float);
   if (FMT == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
   cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), int(smem));
@@ -843,7 +942,11 @@ static cudaError_t launch_gemv_t(const GemvParams &p, dim3 grid, size_t, cudaStr
 }
 
 template <int FMT>
-static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_t smem, cudaStream_t st) {
+static cudaError_t launch_gemv_f(const GemvParams &p, int ncol, dim3 grid, size_t smem, cudaStream_t st, int gs = 0) {
+  if constexpr (FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4) {
+    if (ncol == 1 && gs == 64) return launch_gemv_t<FMT, 1, 64>(p, grid, smem, st);
+    if (ncol == 1 && gs == 128) return launch_gemv_t<FMT, 1, 128>(p, grid, smem, st);
+  }
   switch (ncol) {
     case 1: return launch_gemv_t<FMT, 1>(p, grid, smem, st);
     case 2: return launch_gemv_t<FMT, 2>(p, grid, smem, st);
@@ -917,9 +1020,10 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   size_t smem = size_t(kWarps) * 64 * 16 * sizeof(float);
   if (fmt == LB_FMT_NF4) smem += size_t(kLutWords) * 4;
   const dim3 grid(pl.ctas_x, pl.splits);
+  const int gs = gemv_gs(fmt, p.group, m, k, scales);
   switch (fmt) {
-    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st);
-    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st);
+    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st, gs);
+    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st, gs);
     case LB_FMT_INT8: return launch_gemv_f<LB_FMT_INT8>(p, ncol, grid, smem, st);
     default: return launch_gemv_f<LB_FMT_FP16>(p, ncol, grid, smem, st);
   }
@@ -943,12 +1047,13 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
   const int ncol = m <= 8 ? 1 : 2;
   const int want = std::min(kMaxZSlices, std::max(1, (k / 8 + 31) / 32));
   const int zx = std::max(1, want / pl.splits);
+  const int gs = gemv_gs(fmt, fmt == LB_FMT_FP16 ? k : group, m, k, scales);
   int cap = 0;
   switch (fmt) {
-    case LB_FMT_INT4: cap = resident_ctas_f<LB_FMT_INT4>(ncol); break;
-    case LB_FMT_NF4: cap = resident_ctas_f<LB_FMT_NF4>(ncol); break;
-    case LB_FMT_INT8: cap = resident_ctas_f<LB_FMT_INT8>(ncol); break;
-    default: cap = resident_ctas_f<LB_FMT_FP16>(ncol); break;
+    case LB_FMT_INT4: cap = resident_ctas_f<LB_FMT_INT4>(ncol, gs); break;
+    case LB_FMT_NF4: cap = resident_ctas_f<LB_FMT_NF4>(ncol, gs); break;
+    case LB_FMT_INT8: cap = resident_ctas_f<LB_FMT_INT8>(ncol, gs); break;
+    default: cap = resident_ctas_f<LB_FMT_FP16>(ncol, gs); break;
   }
   if (int64_t(zx + pl.ctas_x) * pl.splits > cap) return cudaSuccess;
   GemvParams p = {};
@@ -985,8 +1090,8 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
   const dim3 grid(pl.ctas_x + zx, pl.splits);
   size_t smem = 0;
   switch (fmt) {
-    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st);
-    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st);
+    case LB_FMT_INT4: return launch_gemv_f<LB_FMT_INT4>(p, ncol, grid, smem, st, gs);
+    case LB_FMT_NF4: return launch_gemv_f<LB_FMT_NF4>(p, ncol, grid, smem, st, gs);
     case LB_FMT_INT8: return launch_gemv_f<LB_FMT_INT8>(p, ncol, grid, smem, st);
     default: return launch_gemv_f<LB_FMT_FP16>(p, ncol, grid, smem, st);
   }

@@ -21,6 +21,15 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// d = A . B with a zero accumulator (the C operand is the constant 0): starts a fresh
+// partial sum, e.g. one scale group's, without zeroing registers first.
+__device__ __forceinline__ void mma16816_zero(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // The lane's 16-byte chunk -> its fp16 pairs, in the format's natural unpack order.
 //   INT4: word w -> (e0,e4) (e1,e5) (e2,e6) (e3,e7) of elements 8w..8w+7
 //   NF4 : byte b of word w -> (e2b, e2b+1)

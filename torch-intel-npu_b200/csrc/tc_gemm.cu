@@ -407,17 +407,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       asm volatile("bar.sync 1, %0;" ::"r"(32 * kDequantWarps));
       if (*is_last) {
         __threadfence();
-        for (int c = chalf * kColsPerWarp; c < (chalf + 1) * kColsPerWarp && c < BM; ++c) {
-          const int m = m0 + c;
-          if (m >= p.m || n >= p.n) continue;
-          float v = 0.f;
-          for (int sp = 0; sp < p.splits; ++sp) v += __ldcg(p.partial + sp * mn + int64_t(m) * p.n + n);
-          __half yq = __float2half_rn(v);
-          if (p.bias) yq = __float2half_rn(__half2float(yq) + bias);
-          if (p.has_corr)
-            yq = __float2half_rn(__half2float(yq) +
-                                 __half2float(__float2half_rn(__ldcg(p.partial + p.splits * mn + int64_t(m) * p.n + n))));
-          p.y[int64_t(m) * p.ldy + n] = yq;
+        // eight output columns at a time: their partial loads are all in flight together
+        // (one L2 round trip per eight columns and split instead of one per column), and
+        // each column's splits are still summed in split order
+        constexpr int kCB = 8;
+        const int c_end = min((chalf + 1) * kColsPerWarp, BM);
+        for (int cb = chalf * kColsPerWarp; cb < c_end; cb += kCB) {
+          float v[kCB], dz[kCB];
+#pragma unroll
+          for (int j = 0; j < kCB; ++j) v[j] = dz[j] = 0.f;
+          const bool any = n < p.n && m0 + cb < p.m;
+          if (any) {
+            for (int sp = 0; sp < p.splits; ++sp) {
+              float part[kCB];
+#pragma unroll
+              for (int j = 0; j < kCB; ++j) {
+                const int m = m0 + cb + j;
+                part[j] = (cb + j < c_end && m < p.m) ? __ldcg(p.partial + sp * mn + int64_t(m) * p.n + n) : 0.f;
+              }
+#pragma unroll
+              for (int j = 0; j < kCB; ++j) v[j] += part[j];
+            }
+            if (p.has_corr) {
+#pragma unroll
+              for (int j = 0; j < kCB; ++j) {
+                const int m = m0 + cb + j;
+                dz[j] = (cb + j < c_end && m < p.m) ? __ldcg(p.partial + p.splits * mn + int64_t(m) * p.n + n) : 0.f;
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kCB; ++j) {
+            const int m = m0 + cb + j;
+            if (!any || cb + j >= c_end || m >= p.m) continue;
+            __half yq = __float2half_rn(v[j]);
+            if (p.bias) yq = __float2half_rn(__half2float(yq) + bias);
+            if (p.has_corr) yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(dz[j])));
+            p.y[int64_t(m) * p.ldy + n] = yq;
+          }
         }
         if (threadIdx.x == 64) p.counters[tile] = 0;
       }
@@ -489,6 +516,10 @@ int tc_block_m(int m) {
 }
 
 int tc_splits(int m, int n, int k) {
+  if (const char *env = getenv("LOWBIT_TC_SPLITS")) {   // tuning: force the K split count
+    const int s = atoi(env);
+    if (s >= 1 && s <= 16) return s;
+  }
   const int bm = tc_block_m(m);
   const int tiles = ((n + 127) / 128) * ((m + bm - 1) / bm);
   const int stages = k / 64;

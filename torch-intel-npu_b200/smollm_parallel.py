@@ -160,4 +160,4 @@ def build_tp_causal_lm(config, layer_weights, embedding, norm, *, mode='nf4a16',
         layers.append(sm.FrozenSmolLayer({k: v for k, v in cfg_r.items() if k != 'tp_world'}, w_r, mode=mode,
                                          packed_weights=p_r, corrections=c_r or None, device=device,
                                          max_positions=max_positions, tp_group=group, row_corrections=row_extra))
-    return sm.SmolForCausalLM(sm.FrozenSmolStack(layers), embedding, norm)
+    return sm.SmolForCausalLM(sm.FrozenSmolStack.from_layers(layers), embedding, norm)

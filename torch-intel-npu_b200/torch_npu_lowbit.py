@@ -101,6 +101,50 @@ class PackedWeight:
         return out.cpu().numpy()
 
 
+@dataclass(frozen=True, eq=False)
+class DevicePackedWeight:
+    """A PackedWeight whose codes and scales already live on a CUDA device (loaded straight
+    there from a packed checkpoint).  Same shape / format / group fields and the same
+    canonical byte layout; no counterpart in the reference, whose packed weights are host
+    bytes compiled into NPU graphs."""
+    shape: tuple
+    format: str
+    group_size: int
+    codes: torch.Tensor
+    scales: torch.Tensor
+
+    def __post_init__(self):
+        if (type(self.shape) is not tuple or len(self.shape) != 2 or any(type(v) is not int or v <= 0 for v in self.shape)
+                or prod(self.shape) > MAX_TENSOR_ELEMENTS or self.format not in ('int4', 'nf4', 'int8')
+                or type(self.group_size) is not int or not 1 <= self.group_size <= self.shape[1]
+                or self.shape[1] % self.group_size):
+            raise ValueError('Weight requires bounded (N,K), int4/nf4/int8, and a group size dividing K')
+        count = prod(self.shape)
+        if (not isinstance(self.codes, torch.Tensor) or self.codes.device.type != 'cuda' or self.codes.dtype != torch.uint8
+                or self.codes.numel() != (count if self.format == 'int8' else (count + 1) // 2)):
+            raise ValueError('Packed weight extent/padding differs')
+        if (not isinstance(self.scales, torch.Tensor) or self.scales.device != self.codes.device
+                or self.scales.dtype != torch.float16 or self.scales.numel() != count // self.group_size):
+            raise ValueError('Scale extent differs')
+        if not bool((torch.isfinite(self.scales) & (self.scales > 0)).all()):
+            raise ValueError('Scales must be finite, positive FP16 values')
+        if self.format != 'int8' and count % 2 and int(self.codes[-1]) & 0xf0:
+            raise ValueError('Packed weight extent/padding differs')
+
+    def to_device(self, device=None):
+        dev = rt.cuda_device(device) if device is not None else self.codes.device
+        return self.codes.to(dev).contiguous(), self.scales.to(dev).contiguous()
+
+    def to_host(self):
+        """The host PackedWeight with the same bytes."""
+        return PackedWeight(self.shape, self.format, self.group_size, self.codes.cpu().numpy().tobytes(),
+                            self.scales.cpu().numpy().tobytes())
+
+    def dequantize(self):
+        n, k = self.shape
+        return rt.dequantize(self.format, self.group_size, n, k, self.codes, self.scales).cpu().numpy()
+
+
 def quantize_weight(weight, *, format='int4', group_size=None):
     """Symmetric per-group quantization with fp16 scales (torch_npu_lowbit.py:78-105), on the GPU.
 

@@ -28,8 +28,9 @@ import torch
 import torch.nn.functional as F
 
 import lowbit_runtime as rt
-from torch_npu_lowbit import PackedWeight, quantize_weight_device
+from torch_npu_lowbit import DevicePackedWeight, PackedWeight, quantize_weight_device
 from torch_npu_lowbit_correction import LowRankCorrection
+from torch_npu_smollm_io import FrozenSmolIO
 
 _STACKS = {'qkv': ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight'),
            'gate_up': ('mlp.gate_proj.weight', 'mlp.up_proj.weight')}
@@ -148,7 +149,7 @@ class FrozenSmolLayer(torch.nn.Module):
             if weight_format is None or type(packed_weights) is not dict or set(packed_weights) != set(_PROJECTIONS):
                 raise ValueError('Prepared weights require all seven projections in a matching lowbit mode')
             for name, q in packed_weights.items():
-                if (not isinstance(q, PackedWeight) or q.shape != shapes[name] or q.format != weight_format
+                if (not isinstance(q, (PackedWeight, DevicePackedWeight)) or q.shape != shapes[name] or q.format != weight_format
                         or (weight_format == 'int8' and q.group_size != shapes[name][1])):
                     raise ValueError('Prepared weights require matching formats/shapes; W8 uses per-row scales')
         rt.require_cuda()
@@ -191,6 +192,29 @@ class FrozenSmolLayer(torch.nn.Module):
 
     mode = property(lambda self: self._mode)
     fp16_projections = property(lambda self: self._fp16_projections)
+
+    @classmethod
+    def from_checkpoint(cls, directory, *, layer_index=0, mode='w8a16', packed_weights=None, fp16_projections=(),
+                        corrections=None, **options):
+        """One layer of a SmolLM safetensors checkpoint directory (torch_npu_smollm.py:119-127);
+        ``options`` are this class's GPU keywords (group_size, device, max_positions)."""
+        from safetensors import safe_open
+        _projection_policy(mode, fp16_projections)
+        directory = Path(directory)
+        config = json.loads((directory / 'config.json').read_text())
+        if type(layer_index) is not int or not 0 <= layer_index < config.get('num_hidden_layers', 0):
+            raise ValueError('Invalid layer index')
+        prefix = f'model.layers.{layer_index}.'
+        with safe_open(directory / 'model.safetensors', framework='pt', device='cpu') as file:
+            weights = {name[len(prefix):]: file.get_tensor(name) for name in file.keys() if name.startswith(prefix)}
+        return cls(config, weights, mode=mode, packed_weights=packed_weights, fp16_projections=fp16_projections,
+                   corrections=corrections, **options)
+
+    def reference_cpu(self, x, *, quantized=True, segment=None, normalized=None):
+        """Not provided: the reference's staged CPU layer (torch_npu_smollm.py:142-193) is its
+        test oracle, and this package has no CPU path -- its restatement lives with the
+        tests, as test infrastructure (oracle/decoder_ref.py in the source tree)."""
+        raise NotImplementedError('reference_cpu is the CPU test oracle; this package runs on the GPU only')
 
     def _stack(self, names):
         """q/k/v (or gate/up) as one decode-GEMV launch (lb_linear_stacked): rows stacked in
@@ -488,39 +512,82 @@ class FrozenSmolLayer(torch.nn.Module):
 
 
 class FrozenSmolStack(torch.nn.Module):
-    """Contiguous decoder layers (torch_npu_smollm.py:558-657)."""
+    """Contiguous decoder layers (torch_npu_smollm.py:558-657).
 
-    def __init__(self, layers):
+    ``FrozenSmolStack(directory, *, start_layer, num_layers, mode, packed_weights,
+    fp16_projections, corrections)`` loads the layer range of a SmolLM safetensors
+    checkpoint directory as the reference does, with the same validation; the GPU
+    keywords ``group_size``, ``device`` and ``max_positions`` are passed to every layer.
+    ``packed_weights`` / ``corrections`` are maps indexed by checkpoint layer, e.g. as
+    read by torch_npu_lowbit_checkpoint.load_packed.  Corrections are accepted for every
+    quantized mode (the reference: W8 with explicit packed weights only).
+    ``FrozenSmolStack.from_layers(layers)`` wraps layers built in memory (no reference
+    counterpart).
+    """
+
+    def __init__(self, directory, *, start_layer=0, num_layers=2, mode='w8a16', packed_weights=None,
+                 fp16_projections=(), corrections=None, group_size=None, device=None, max_positions=None):
         super().__init__()
-        if not layers or any(not isinstance(l, FrozenSmolLayer) for l in layers):
-            raise ValueError('Requires a nonempty list of FrozenSmolLayer')
-        self.layers = torch.nn.ModuleList(layers)
-        self.eval()
-
-    @classmethod
-    def from_checkpoint(cls, directory, *, start_layer=0, num_layers=2, mode='w8a16', packed_weights=None,
-                        fp16_projections=(), corrections=None, group_size=None, device=None):
-        """Load layers from a SmolLM safetensors checkpoint directory (config.json + model.safetensors)."""
-        _projection_policy(mode, fp16_projections)
-        from safetensors import safe_open
+        self._fp16_projections = _projection_policy(mode, fp16_projections)
         directory = Path(directory)
         config = json.loads((directory / 'config.json').read_text())
         total = config.get('num_hidden_layers', 0)
-        if (type(start_layer) is not int or type(num_layers) is not int or start_layer < 0 or num_layers <= 0
-                or start_layer + num_layers > total):
+        if (type(start_layer) is not int or type(num_layers) is not int or type(total) is not int
+                or start_layer < 0 or num_layers <= 0 or start_layer + num_layers > total):
             raise ValueError('Requires a nonempty contiguous checkpoint layer range')
+        if mode not in _WEIGHT_FORMATS:
+            raise ValueError('Requires fp16, w8a16, w4a16 or nf4a16')
+        indices = set(range(start_layer, start_layer + num_layers))
+        if packed_weights is not None and (mode == 'fp16' or type(packed_weights) is not dict
+                                           or any(type(i) is not int for i in packed_weights)
+                                           or any(type(v) is not dict for v in packed_weights.values())
+                                           or set(packed_weights) != indices):
+            raise ValueError('Prepared stack weights require a complete lowbit map indexed by checkpoint layer')
+        if corrections is not None and (mode == 'fp16' or type(corrections) is not dict
+                                        or any(type(i) is not int or type(v) is not dict for i, v in corrections.items())
+                                        or set(corrections) != indices):
+            raise ValueError('Stack corrections require a quantized mode and a complete map indexed by checkpoint layer')
+        from safetensors import safe_open
         layers = []
-        with safe_open(directory / 'model.safetensors', framework='pt', device='cpu') as f:
-            names = list(f.keys())
+        with safe_open(directory / 'model.safetensors', framework='pt', device='cpu') as file:
+            names = list(file.keys())
             for i in range(start_layer, start_layer + num_layers):
                 prefix = f'model.layers.{i}.'
-                weights = {n[len(prefix):]: f.get_tensor(n) for n in names if n.startswith(prefix)}
+                weights = {n[len(prefix):]: file.get_tensor(n) for n in names if n.startswith(prefix)}
                 layers.append(FrozenSmolLayer(config, weights, mode=mode,
                                               packed_weights=None if packed_weights is None else packed_weights[i],
                                               fp16_projections=fp16_projections,
                                               corrections=None if corrections is None else corrections[i],
-                                              group_size=group_size, device=device))
-        return cls(layers)
+                                              group_size=group_size, device=device, max_positions=max_positions))
+        self._set_layers(layers, start_layer, mode)
+
+    def _set_layers(self, layers, start_layer, mode):
+        self.layers = torch.nn.ModuleList(layers)
+        self.start_layer = start_layer
+        self._mode = mode
+        self.eval()
+
+    @classmethod
+    def from_layers(cls, layers, *, start_layer=0):
+        """A stack of layers already built in memory."""
+        if not layers or any(not isinstance(l, FrozenSmolLayer) for l in layers):
+            raise ValueError('Requires a nonempty list of FrozenSmolLayer')
+        self = cls.__new__(cls)
+        torch.nn.Module.__init__(self)
+        self._fp16_projections = layers[0].fp16_projections
+        self._set_layers(layers, start_layer, layers[0].mode)
+        return self
+
+    @classmethod
+    def from_checkpoint(cls, directory, **options):
+        return cls(directory, **options)
+
+    mode = property(lambda self: self._mode)
+    fp16_projections = property(lambda self: self._fp16_projections)
+
+    def reference_cpu(self, x, *, quantized=True):
+        """Not provided (see FrozenSmolLayer.reference_cpu)."""
+        raise NotImplementedError('reference_cpu is the CPU test oracle; this package runs on the GPU only')
 
     @property
     def num_layers(self):
@@ -554,11 +621,11 @@ class FrozenSmolStack(torch.nn.Module):
 
 
 class SmolForCausalLM(torch.nn.Module):
-    """Decoder stack + tied fp16 embedding / LM head with greedy generation.
+    """Decoder stack + tied fp16 embedding / LM head (FrozenSmolIO) with greedy generation.
 
-    The embedding lookup and final norm follow FrozenSmolIO (torch_npu_smollm_io.py:45-61);
-    the decode step (all layers + head + argmax) is captured once per batch size in a
-    CUDA graph and replayed per token.
+    The decode step (all layers + head + argmax) is captured once per batch size in a
+    CUDA graph and replayed per token.  No reference counterpart: the reference drives its
+    stack and FrozenSmolIO from the caller (torch_npu_smollm_io.py:14-61).
     """
 
     def __init__(self, stack, embedding, norm):
@@ -566,29 +633,36 @@ class SmolForCausalLM(torch.nn.Module):
         self.stack = stack
         self.config = stack.layers[0].config
         self.device = stack.layers[0].device
-        self.embedding = embedding.detach().to(self.device, torch.float16).contiguous()
-        self.final_norm = norm.detach().to(self.device, torch.float16).contiguous()
+        cfg = dict(model_type='llama', hidden_size=self.config.hidden, vocab_size=self.config.vocab,
+                   tie_word_embeddings=True, rms_norm_eps=self.config.eps)
+        self.io = FrozenSmolIO(cfg, embedding, norm, device=self.device)
+        self.embedding = self.io.embedding
+        self.final_norm = self.io.norm
         self._graphs = {}
 
     @classmethod
     def from_weights(cls, config, layer_weights, embedding, norm, **layer_options):
         layers = [FrozenSmolLayer(config, w, **layer_options) for w in layer_weights]
-        return cls(FrozenSmolStack(layers), embedding, norm)
+        return cls(FrozenSmolStack.from_layers(layers), embedding, norm)
+
+    @classmethod
+    def from_checkpoint(cls, directory, **stack_options):
+        """Every layer of a SmolLM checkpoint directory plus its tied endpoints; the options
+        are FrozenSmolStack's (mode, packed_weights, corrections, group_size, ...)."""
+        from safetensors import safe_open
+        directory = Path(directory)
+        total = json.loads((directory / 'config.json').read_text()).get('num_hidden_layers', 0)
+        stack = FrozenSmolStack(directory, start_layer=0, num_layers=total, **stack_options)
+        with safe_open(directory / 'model.safetensors', framework='pt', device='cpu') as f:
+            emb, norm = f.get_tensor('model.embed_tokens.weight'), f.get_tensor('model.norm.weight')
+        return cls(stack, emb, norm)
 
     def embed(self, ids):
-        t = ids.numel()
-        out = torch.empty(t, self.config.hidden, dtype=torch.float16, device=self.device)
-        rt.check(rt.lib().lb_embed(rt.ptr(ids), rt.ptr(self.embedding), rt.ptr(out), t, self.config.hidden,
-                                   self.config.vocab, rt.stream_ptr(self.device)), 'lb_embed')
-        return out
+        return self.io.embed_rows(ids)
 
     def head(self, h, residual=None):
         """Final RMSNorm (fused with the last residual add) + tied LM head -> fp16 logits."""
-        normed = torch.empty_like(h)
-        res_out = torch.empty_like(h) if residual is not None else None
-        rt.check(rt.lib().lb_rmsnorm(rt.ptr(h), rt.ptr(residual), rt.ptr(res_out), rt.ptr(self.final_norm), rt.ptr(normed),
-                                     h.shape[0], h.shape[1], self.config.eps, rt.stream_ptr(self.device)), 'lb_rmsnorm')
-        return rt.linear(normed, 'fp16', self.config.hidden, self.config.vocab, self.embedding.view(torch.uint8).reshape(-1), None)
+        return self.io.head_rows(h, residual)
 
     def argmax(self, logits, out):
         rt.check(rt.lib().lb_argmax(rt.ptr(logits), logits.shape[0], logits.shape[1], rt.ptr(out), None, 0,
