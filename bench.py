@@ -763,32 +763,70 @@ def run_reference(args):
 
 
 def profile_case(which):
-    """Small, self-contained workloads for ncu captures (committed, so that a capture
-    runs committed files only).  dominant: the NF4 g64 8192x2048
-    decode GEMV (M=1) over 16 weight replicas (144 MB, larger than L2), 48 launches;
-    prefill: the same layer at M=2048 with the rank-32 correction on the tensor-core
-    path, 6 launches."""
+    """Small, self-contained workloads for ncu captures (committed, so that a capture runs
+    committed files only); each holds a few GB on the device at most.
+      dominant  -- the NF4 g64 8192x2048 decode GEMV (M=1) over 16 weight replicas (144 MB,
+                   larger than L2), 48 launches;
+      prefill   -- the same layer at M=2048 with the rank-32 correction on the tcgen05 path,
+                   6 launches;
+      batched   -- the same layer at M=64 with the correction (batched-decode GEMV), 12
+                   launches over 4 replicas;
+      attention -- one-token GQA attention of configs[4] at batch 32 (32 heads / 32 KV heads,
+                   2176 cached positions, 570 MB of K/V), 4 launches;
+      quantize  -- NF4 g64 quantize + pack of a 8192x2048 fp16 weight, 3 launches;
+      decode    -- one greedy decode step of two configs[4] layers (+ head) at batch 32,
+                   replayed 3 times."""
     import lowbit_runtime as rt
     rt.require_cuda()
     fmt, g, n, k = DOMINANT
     gen = torch.Generator(device='cpu').manual_seed(3)
-    reps = 16 if which == 'dominant' else 2
-    packed = [rt.quantize_pack((torch.randn(n, k, generator=gen) * 0.02).half().cuda(), fmt, g) for _ in range(reps)]
-    m = 1 if which == 'dominant' else 2048
-    x = torch.randn(m, k, generator=gen).half().cuda()
-    v = (torch.randn(RANK, k, generator=gen) * 1e-3).half().cuda()
-    u = (torch.randn(n, RANK, generator=gen) * 1e-3).half().cuda()
-    y = torch.empty(m, n, dtype=torch.float16, device='cuda')
-    launches = 48 if which == 'dominant' else 6
-    for i in range(launches):
-        c, sc = packed[i % reps]
-        if which == 'dominant':
-            rt.linear(x, fmt, g, n, c, sc, out=y)
-        else:
-            rt.linear(x, fmt, g, n, c, sc, down=v, up=u, out=y)
+    info = {'profile_case': which}
+    if which in ('dominant', 'prefill', 'batched'):
+        reps = {'dominant': 16, 'prefill': 2, 'batched': 4}[which]
+        packed = [rt.quantize_pack((torch.randn(n, k, generator=gen) * 0.02).half().cuda(), fmt, g) for _ in range(reps)]
+        m = {'dominant': 1, 'prefill': 2048, 'batched': 64}[which]
+        x = torch.randn(m, k, generator=gen).half().cuda()
+        v = (torch.randn(RANK, k, generator=gen) * 1e-3).half().cuda()
+        u = (torch.randn(n, RANK, generator=gen) * 1e-3).half().cuda()
+        y = torch.empty(m, n, dtype=torch.float16, device='cuda')
+        launches = {'dominant': 48, 'prefill': 6, 'batched': 12}[which]
+        for i in range(launches):
+            c, sc = packed[i % reps]
+            if which == 'dominant':
+                rt.linear(x, fmt, g, n, c, sc, out=y)
+            else:
+                rt.linear(x, fmt, g, n, c, sc, down=v, up=u, out=y)
+        info.update(launches=launches, m=m, n=n, k=k, format=fmt, group=g)
+    elif which == 'attention':
+        b, heads, kvh, hd, max_pos = 32, 32, 32, 64, 2176
+        L = rt.lib()
+        q = torch.randn(b, heads * hd, generator=gen).half().cuda()
+        kc = (torch.randn(b, kvh, max_pos, hd, generator=gen) * 0.5).half().cuda()
+        vc = (torch.randn(b, kvh, max_pos, hd, generator=gen) * 0.5).half().cuda()
+        lengths = torch.full((b,), max_pos - 1, dtype=torch.int32, device='cuda')
+        out = torch.empty(b, heads * hd, dtype=torch.float16, device='cuda')
+        ws = rt.Workspace.get(L.lb_attention_workspace_bytes(b, heads, max_pos))
+        for _ in range(4):
+            rt.check(L.lb_attention_decode(rt.ptr(q), heads * hd, rt.ptr(kc), rt.ptr(vc), rt.ptr(lengths), rt.ptr(out),
+                                           b, heads, kvh, hd, max_pos, 0.125, rt.ptr(ws), ws.numel(), rt.stream_ptr()),
+                     'lb_attention_decode')
+        info.update(batch=b, heads=heads, kv_heads=kvh, positions=max_pos, kv_bytes=2 * b * kvh * max_pos * hd * 2)
+    elif which == 'quantize':
+        w = (torch.randn(n, k, generator=gen) * 0.02).half().cuda()
+        for _ in range(3):
+            rt.quantize_pack(w, fmt, g)
+        info.update(n=n, k=k, format=fmt, group=g)
+    elif which == 'decode':
+        m = build_smollm('1.7b', 'nf4a16', 64, torch.device('cuda'), 64 + 16, layers=2)
+        ids = torch.randint(0, m.config.vocab, (32, 64), generator=gen).cuda()
+        m.prefill_session(ids)
+        for _ in range(3):
+            m.decode_step(32)
+        info.update(layers=2, batch=32, prompt=64, launches_per_step=graph_kernel_nodes(m.session(32)['graph']))
+    else:
+        raise ValueError(which)
     torch.cuda.synchronize()
-    print(json.dumps({'profile_case': which, 'launches': launches, 'm': m, 'n': n, 'k': k, 'format': fmt,
-                      'group': g, 'checksum': float(y.float().abs().sum())}), flush=True)
+    print(json.dumps(info), flush=True)
     return 0
 
 
@@ -801,7 +839,7 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decode', action='store_true')
     ap.add_argument('--quick-decode', action='store_true')
-    ap.add_argument('--profile', choices=['dominant', 'prefill'],
+    ap.add_argument('--profile', choices=['dominant', 'prefill', 'batched', 'attention', 'quantize', 'decode'],
                     help='run a small fixed workload for an ncu capture and exit')
     args = ap.parse_args()
     if args.profile:

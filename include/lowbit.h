@@ -188,9 +188,15 @@ int lb_rope(uint16_t *q, uint16_t *k, const int32_t *positions, const uint16_t *
 int lb_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *k_cache,
                  uint16_t *v_cache, const int32_t *lengths, int batch, int kv_heads, int head_dim,
                  int max_pos, void *stream);
-/* One-query GQA attention over the cache, staging of torch_npu_smollm.py:178-182:
- * s = half(half(q.k) * scale); p = half(softmax_f32(s)); out = half(p . v).
- * Attends positions 0..lengths[b] (inclusive).  out [B, heads*hd]. */
+/* One-query GQA attention over the cache (torch_npu_smollm.py:178-182, the KV Select and
+ * attention of :262-301): s = half(half(q.k) * scale), softmax in fp32 as an online
+ * (running max / sum) pass, out = half(p . v) -- the reference rounds p to fp16 before
+ * p . v, here p stays fp32.  Attends positions 0..lengths[b] (inclusive).  out
+ * [B, heads*hd].  When batch x kv_heads gives too few CTAs, the positions of each
+ * (sequence, kv head) are split across CTAs and merged in split order (deterministic);
+ * the splits need `workspace` (lb_attention_workspace_bytes; it may be the same buffer
+ * as a linear workspace on the same stream -- the arrival counters are shared and left at
+ * zero).  A NULL or smaller workspace only reduces the splits. */
 int lb_attention_decode(const uint16_t *q, int q_stride, const uint16_t *k_cache,
                         const uint16_t *v_cache, const int32_t *lengths, uint16_t *out, int batch,
                         int heads, int kv_heads, int head_dim, int max_pos, float scale,
@@ -201,13 +207,14 @@ size_t lb_attention_workspace_bytes(int batch, int heads, int max_pos);
  * of (b, kv head) rotates and appends that head's new k row (and copies v) at position
  * lengths[b], then rotates q while loading it; same fp16 staging as the three calls.
  * k_new / v_new: [B, kv_stride] rows (column blocks of one q|k|v buffer allowed); q is
- * read, not written.  Positions at or past table_rows are attended unrotated. */
+ * read, not written.  Positions at or past table_rows are attended unrotated.  Workspace
+ * as for lb_attention_decode. */
 int lb_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new,
                              const uint16_t *v_new, int kv_stride, const uint16_t *cos_table,
                              const uint16_t *sin_table, int table_rows, uint16_t *k_cache,
                              uint16_t *v_cache, const int32_t *lengths, uint16_t *out, int batch,
                              int heads, int kv_heads, int head_dim, int max_pos, float scale,
-                             void *stream);
+                             void *workspace, size_t workspace_bytes, void *stream);
 /* h = half(half(silu(float(gate))) * up)  (torch_npu_smollm.py:189-190); gate/up may be
  * column blocks of one [rows, 2F] buffer (row stride in elements). */
 int lb_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows,

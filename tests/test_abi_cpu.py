@@ -44,7 +44,7 @@ def test_runtime_binds_the_whole_header():
 
 
 def test_status_strings_and_version(lib):
-    assert lib.lb_abi_version() == 1
+    assert lib.lb_abi_version() == 2
     assert lib.lb_status_string(0) == b'ok'
     assert b'Nonfinite' in lib.lb_status_string(4)
     assert lib.lb_status_string(12345) == b'unknown status'

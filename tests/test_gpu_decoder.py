@@ -156,17 +156,40 @@ def test_generate_matches_oracle(config, mode, group, corrected):
 ], ids=['360m-int4-g128/64-b2', '360m-nf4-g64-b2', '1.7b-nf4-g64-b2', '360m-int4-b64', '1.7b-nf4-b32'])
 def test_generate_at_baseline_dims_matches_oracle(config, mode, group, batch, steps):
     """BASELINE configs[3] and [4] at their layer dimensions (two layers, rank-32
-    corrections on every projection, a 16-token prompt): logits within 0.5% relative L2
-    of the same-format oracle and identical greedy tokens, at batch 2 for 32 steps and at
-    the benchmark's own decode batches (64 for 360M, 32 for 1.7B), whose GEMV column
-    counts and attention grids differ from batch 2."""
+    corrections on every projection, a 16-token prompt), through the decode path the
+    benchmark times (prefill, then the replayed decode-step graph):
+
+    * batch 2, 32 steps, free-running: logits within 0.5% relative L2 of the same-format
+      oracle and identical greedy tokens;
+    * the benchmark's own decode batches (64 for 360M, 32 for 1.7B; other GEMV column
+      counts and attention grids), 8 steps with the oracle's tokens fed to both models:
+      logits within 0.5% at every step, and the greedy token equal wherever the oracle's
+      top-two logit gap exceeds twice that step's largest logit difference (a closer gap
+      is a near-tie that fp16 rounding order may break either way; with 32-64 random-init
+      sequences some occur)."""
     model, oracle = build(config, mode, group, True, seed=11)
     ids = torch.randint(0, config['vocab_size'], (batch, 16), generator=torch.Generator().manual_seed(6))
-    tokens, logits = model.generate(ids.cuda(), steps, return_logits=True)
     etokens, elogits = oracle.generate(ids, steps)
-    errs = [rel_l2(logits[t], elogits[t]) for t in range(steps)]
-    assert max(errs) < LOGIT_L2, errs
-    assert torch.equal(tokens.cpu(), etokens), (tokens.cpu(), etokens)
+    if batch <= 2:
+        tokens, logits = model.generate(ids.cuda(), steps, return_logits=True)
+        errs = [rel_l2(logits[t], elogits[t]) for t in range(steps)]
+        assert max(errs) < LOGIT_L2, errs
+        assert torch.equal(tokens.cpu(), etokens), (tokens.cpu(), etokens)
+        return
+    st = model.session(batch)
+    logits = [model.prefill_session(ids.cuda()).clone()]
+    for t in range(1, steps):
+        st['ids'].copy_(etokens[:, t - 1].cuda())
+        logits.append(model.decode_step(batch).clone())
+    checked = 0
+    for t in range(steps):
+        got, exp = logits[t].float().cpu(), elogits[t].float()
+        assert rel_l2(got, exp) < LOGIT_L2, (t, rel_l2(got, exp))
+        top2 = exp.topk(2, dim=-1).values
+        decided = (top2[:, 0] - top2[:, 1]) > 2 * (got - exp).abs().max(-1).values
+        assert torch.equal(got.argmax(-1)[decided], etokens[:, t][decided]), t
+        checked += int(decided.sum())
+    assert checked >= 0.9 * batch * steps, checked
 
 
 def test_graph_replay_equals_eager():
@@ -245,15 +268,17 @@ def test_fused_rope_append_attention_equals_separate_calls(heads, kv, b):
     rt.check(L.lb_kv_append(rt.ptr(k1), rt.ptr(v1), sep.stride(0), rt.ptr(kc1), rt.ptr(vc1), rt.ptr(lengths), b, kv, hd,
                             max_pos, st), 'lb_kv_append')
     out1 = torch.empty(b, nq, dtype=torch.float16, device='cuda')
+    ws = rt.Workspace.get(L.lb_attention_workspace_bytes(b, heads, max_pos))
     rt.check(L.lb_attention_decode(rt.ptr(q1), sep.stride(0), rt.ptr(kc1), rt.ptr(vc1), rt.ptr(lengths), rt.ptr(out1), b,
-                                   heads, kv, hd, max_pos, scale, None, 0, st), 'lb_attention_decode')
+                                   heads, kv, hd, max_pos, scale, rt.ptr(ws), ws.numel(), st), 'lb_attention_decode')
     # fused
     kc2, vc2 = caches[0].clone(), caches[1].clone()
     q2, k2, v2 = qkv[:, :nq], qkv[:, nq:nq + nk], qkv[:, nq + nk:]
     out2 = torch.empty(b, nq, dtype=torch.float16, device='cuda')
     rt.check(L.lb_attention_decode_rope(rt.ptr(q2), qkv.stride(0), rt.ptr(k2), rt.ptr(v2), qkv.stride(0), rt.ptr(cos),
                                         rt.ptr(sin), cos.shape[0], rt.ptr(kc2), rt.ptr(vc2), rt.ptr(lengths), rt.ptr(out2),
-                                        b, heads, kv, hd, max_pos, scale, st), 'lb_attention_decode_rope')
+                                        b, heads, kv, hd, max_pos, scale, rt.ptr(ws), ws.numel(), st),
+             'lb_attention_decode_rope')
     torch.cuda.synchronize()
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
     assert torch.equal(out1, out2)
@@ -297,3 +322,41 @@ def test_row_project_ops_equal_separate_ops(rows, dim, rank):
     if rank:
         exact = (act.double() @ down.double().t())
         assert float((z[:, :rank].double() - exact).abs().max()) <= 2 ** -10 * float(exact.abs().max()) + 1e-3
+
+
+@pytest.mark.parametrize('heads,kv,b,max_pos,splits', [(32, 32, 2, 2304, None), (32, 8, 4, 2304, '7'),
+                                                       (15, 5, 3, 640, '1'), (15, 5, 3, 640, '16'), (9, 3, 1, 96, None)])
+def test_attention_position_splits_match_the_reference_staging(monkeypatch, heads, kv, b, max_pos, splits):
+    """lb_attention_decode against a torch fp32 statement of torch_npu_smollm.py:178-182
+    (scores half(half(q.k) * scale), fp32 softmax, p rounded to fp16, p.V) over ragged
+    lengths, with the positions of each (sequence, kv head) split across CTAs (forced or
+    chosen); the splits' merge keeps the result within fp16 rounding of the reference."""
+    import lowbit_runtime as rt
+    if splits:
+        monkeypatch.setenv('LOWBIT_ATTN_SPLITS', splits)
+    L, st = rt.lib(), rt.stream_ptr()
+    hd, rep = 64, heads // kv
+    gen = torch.Generator().manual_seed(heads * 7 + b)
+    q = (torch.randn(b, heads * hd, generator=gen)).half()
+    kc = (torch.randn(b, kv, max_pos, hd, generator=gen) * 0.5).half()
+    vc = (torch.randn(b, kv, max_pos, hd, generator=gen) * 0.5).half()
+    lengths = torch.randint(0, max_pos, (b,), generator=gen, dtype=torch.int32)
+    lengths[0] = max_pos - 1
+    scale = 1.0 / hd ** 0.5
+    out = torch.empty(b, heads * hd, dtype=torch.float16, device='cuda')
+    ws = rt.Workspace.get(L.lb_attention_workspace_bytes(b, heads, max_pos))
+    qd, kd, vd, ld = q.cuda(), kc.cuda(), vc.cuda(), lengths.cuda()   # alive until the kernel has run
+    rt.check(L.lb_attention_decode(rt.ptr(qd), heads * hd, rt.ptr(kd), rt.ptr(vd), rt.ptr(ld), rt.ptr(out), b, heads,
+                                   kv, hd, max_pos, scale, rt.ptr(ws), ws.numel(), st), 'lb_attention_decode')
+    torch.cuda.synchronize()
+    for i in range(b):
+        n = int(lengths[i]) + 1
+        qi = q[i].view(heads, 1, hd).float()
+        k = kc[i, :, :n].repeat_interleave(rep, 0).float()
+        v = vc[i, :, :n].repeat_interleave(rep, 0).float()
+        s = (qi @ k.transpose(1, 2)).half()
+        s = (s * scale).half()
+        p = s.float().softmax(-1).half()
+        ref_out = (p.float() @ v).half().view(-1).float()
+        got = out[i].float().cpu()
+        assert float((got - ref_out).abs().max()) <= 2e-3 * float(ref_out.abs().max()) + 1e-3, (i, n)

@@ -48,17 +48,19 @@ cudaError_t launch_rope(uint16_t *q, uint16_t *k, const int32_t *pos, const uint
                         cudaStream_t st);
 cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *kc, uint16_t *vc,
                              const int32_t *lengths, int batch, int kvh, int hd, int max_pos, cudaStream_t st);
-size_t attention_smem(int heads, int kvh, int max_pos);
+size_t attention_scratch_bytes(int batch, int heads, int splits);
 cudaError_t launch_row_project(int mode, const uint16_t *x, const uint16_t *res, uint16_t *res_out,
                                const uint16_t *gamma, uint16_t *out, int rows, int dim, int in_stride, float eps,
                                const uint16_t *v, int rank, uint16_t *z, cudaStream_t st);
 cudaError_t launch_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
                                          int kv_stride, const uint16_t *cos_t, const uint16_t *sin_t, int table_rows,
                                          uint16_t *kc, uint16_t *vc, const int32_t *lengths, uint16_t *out, int batch,
-                                         int heads, int kvh, int hd, int max_pos, float scale, cudaStream_t st);
+                                         int heads, int kvh, int hd, int max_pos, float scale, int *counters,
+                                         void *scratch, size_t scratch_bytes, cudaStream_t st);
 cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
                                     const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
-                                    int max_pos, float scale, cudaStream_t st);
+                                    int max_pos, float scale, int *counters, void *scratch, size_t scratch_bytes,
+                                    cudaStream_t st);
 cudaError_t launch_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,
                             cudaStream_t st);
 cudaError_t launch_add(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t count, cudaStream_t st);
@@ -203,7 +205,7 @@ const char *lb_status_string(int s) {
   }
 }
 
-int lb_abi_version(void) { return 1; }
+int lb_abi_version(void) { return 2; }
 
 int lb_last_cuda_error(void) { return g_last_cuda_error; }
 
@@ -443,41 +445,76 @@ int lb_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride, uint16_t *
                                       static_cast<cudaStream_t>(stream)));
 }
 
-size_t lb_attention_workspace_bytes(int, int, int) { return 0; }
+size_t lb_attention_workspace_bytes(int batch, int heads, int max_pos) {
+  if (batch < 1 || heads < 1 || max_pos < 1) return kHeader;
+  return kHeader + attention_scratch_bytes(batch, heads, 16);
+}
+
+namespace {
+// Attention workspace: the linear workspace's arrival counters (the same header, so one
+// buffer can serve both on a stream) and the position-split scratch after it.  A missing
+// or short workspace only limits the splits.
+void attention_ws(void *workspace, size_t workspace_bytes, int **counters, void **scratch, size_t *scratch_bytes) {
+  *counters = nullptr;
+  *scratch = nullptr;
+  *scratch_bytes = 0;
+  if (workspace && workspace_bytes > kHeader && aligned16(workspace)) {
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    *counters = reinterpret_cast<int *>(ws + kCounterOffset);
+    *scratch = ws + kHeader;
+    *scratch_bytes = workspace_bytes - kHeader;
+  }
+}
+
+bool attention_shape_ok(int batch, int heads, int kv_heads, int head_dim, int max_pos) {
+  return batch >= 1 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && heads / kv_heads <= 8 &&
+         head_dim == 64 && max_pos >= 1 && int64_t(batch) * kv_heads * max_pos <= (int64_t(1) << 31);
+}
+}  // namespace
 
 int lb_attention_decode(const uint16_t *q, int q_stride, const uint16_t *k_cache, const uint16_t *v_cache,
                         const int32_t *lengths, uint16_t *out, int batch, int heads, int kv_heads, int head_dim,
-                        int max_pos, float scale, void *, size_t, void *stream) {
+                        int max_pos, float scale, void *workspace, size_t workspace_bytes, void *stream) {
   if (injected("lb_attention_decode")) return LB_ERR_INJECTED;
-  if (!q || !k_cache || !v_cache || !lengths || !out || batch < 1 || heads < 1 || kv_heads < 1 || heads % kv_heads ||
-      heads / kv_heads > 8 || head_dim != 64 || max_pos < 1 || q_stride < heads * head_dim ||
-      attention_smem(heads, kv_heads, max_pos) > 160 * 1024)
+  if (!q || !k_cache || !v_cache || !lengths || !out || !attention_shape_ok(batch, heads, kv_heads, head_dim, max_pos) ||
+      q_stride < heads * head_dim)
     return LB_ERR_INVALID_ARGUMENT;
   if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q) || q_stride % 8) return LB_ERR_INVALID_ARGUMENT;
+  int *counters;
+  void *scratch;
+  size_t sb;
+  attention_ws(workspace, workspace_bytes, &counters, &scratch, &sb);
   return cuda_status(launch_attention_decode(q, q_stride, k_cache, v_cache, lengths, out, batch, heads, kv_heads,
-                                             head_dim, max_pos, scale, static_cast<cudaStream_t>(stream)));
+                                             head_dim, max_pos, scale, counters, scratch, sb,
+                                             static_cast<cudaStream_t>(stream)));
 }
 
 int lb_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
                              int kv_stride, const uint16_t *cos_table, const uint16_t *sin_table, int table_rows,
                              uint16_t *k_cache, uint16_t *v_cache, const int32_t *lengths, uint16_t *out, int batch,
-                             int heads, int kv_heads, int head_dim, int max_pos, float scale, void *stream) {
+                             int heads, int kv_heads, int head_dim, int max_pos, float scale, void *workspace,
+                             size_t workspace_bytes, void *stream) {
   if (injected("lb_attention_decode_rope")) return LB_ERR_INJECTED;
-  if (!q || !k_new || !v_new || !cos_table || !sin_table || !k_cache || !v_cache || !lengths || !out || batch < 1 ||
-      heads < 1 || kv_heads < 1 || heads % kv_heads || heads / kv_heads > 8 || head_dim != 64 || max_pos < 1 ||
-      table_rows < 1 || q_stride < heads * head_dim || kv_stride < kv_heads * head_dim ||
-      attention_smem(heads, kv_heads, max_pos) > 160 * 1024)
+  if (!q || !k_new || !v_new || !cos_table || !sin_table || !k_cache || !v_cache || !lengths || !out ||
+      !attention_shape_ok(batch, heads, kv_heads, head_dim, max_pos) || table_rows < 1 ||
+      q_stride < heads * head_dim || kv_stride < kv_heads * head_dim)
     return LB_ERR_INVALID_ARGUMENT;
   if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q) || q_stride % 8) return LB_ERR_INVALID_ARGUMENT;
   // strided row blocks: the last row ends width elements after its start
   const size_t ob = size_t(batch) * heads * head_dim * 2;
   const size_t qb = (size_t(batch - 1) * q_stride + size_t(heads) * head_dim) * 2;
   const size_t kb = (size_t(batch - 1) * kv_stride + size_t(kv_heads) * head_dim) * 2;
-  if (overlaps(out, ob, q, qb) || overlaps(out, ob, k_new, kb) || overlaps(out, ob, v_new, kb))
+  if (overlaps(out, ob, q, qb) || overlaps(out, ob, k_new, kb) || overlaps(out, ob, v_new, kb) ||
+      overlaps(out, ob, workspace, workspace_bytes))
     return LB_ERR_ALIAS;
+  int *counters;
+  void *scratch;
+  size_t sb;
+  attention_ws(workspace, workspace_bytes, &counters, &scratch, &sb);
   return cuda_status(launch_attention_decode_rope(q, q_stride, k_new, v_new, kv_stride, cos_table, sin_table,
                                                   table_rows, k_cache, v_cache, lengths, out, batch, heads, kv_heads,
-                                                  head_dim, max_pos, scale, static_cast<cudaStream_t>(stream)));
+                                                  head_dim, max_pos, scale, counters, scratch, sb,
+                                                  static_cast<cudaStream_t>(stream)));
 }
 
 namespace {

@@ -1,6 +1,9 @@
 // SmolLM decoder ops around the low-bit projections, following the staged fp16
 // rounding of FrozenSmolLayer.reference_cpu (torch_npu_smollm.py:142-193) and
 // FrozenSmolIO (torch_npu_smollm_io.py:45-61).  All HBM-bound, one pass each.
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace lowbit {
@@ -137,11 +140,30 @@ struct RopeAppend {
   int table_rows;
 };
 
-// One-token GQA attention with the reference staging (torch_npu_smollm.py:178-182):
-// s_j = half(half(q.k_j) * scale); p = half(softmax_f32(s)); out = half(sum_j p_j v_j).
-// One CTA per (batch, kv head) serving the REP query heads that share it.  Keys and values
-// are read as 16-byte pieces (8 lanes per 128-byte row, 4 rows per warp) with kUnroll rows
-// per lane in flight, so a CTA keeps ~128 rows of loads outstanding per phase.
+// Position splits of one (sequence, kv head): scratch for each split's softmax state.
+struct AttnSplit {
+  float *part;     // [B * kvh][splits][REP][2 + HD] fp32: running max, sum, unnormalised p.V
+  int *counters;   // [B * kvh] arrival counters, zero between calls (the last CTA resets)
+};
+
+// (m, l, a) <- the softmax state of two disjoint position sets merged: m the larger max,
+// l and a rescaled by exp(m_i - m); an empty set (m = -inf) contributes nothing.
+__device__ __forceinline__ float softmax_weight(float mi, float m) { return mi == -INFINITY ? 0.f : expf(mi - m); }
+
+// One-token GQA attention, one pass over the cache (torch_npu_smollm.py:178-182):
+// s_j = half(half(q.k_j) * scale) as the reference stages it, then an online softmax --
+// each 8-lane group keeps the running max m, sum l = sum_j exp(s_j - m) and
+// a = sum_j exp(s_j - m) v_j (fp32) over the rows it reads -- merged across the groups of
+// a warp, the warps of the CTA and, when the positions are split across CTAs, the splits
+// (the last CTA of a (sequence, kv head) to finish merges them in split order, so the
+// result does not depend on timing); out = half(a / l).  The reference rounds
+// p_j = exp(s_j - max) / sum to fp16 before p.V; here p stays fp32 (a relative
+// difference of at most 2^-11 per term).
+// Grid (B * kvh, splits); split s reads positions [s * per, (s + 1) * per), per a
+// multiple of 16.  Keys and values are read as 16-byte pieces (8 lanes per 128-byte row,
+// 4 rows per warp, 4 rows per lane in flight): a warp step reads the K and V rows of 16
+// positions.  The optional prologue (RoPE of q and the new k, KV append) is done by the
+// split that owns the appended position -- no other split reads it.
 template <int HD, int REP>
 // kc / vc are written by the prologue and read back in the same kernel, so they are not
 // declared read-only (no non-coherent loads of the appended row).
@@ -149,26 +171,31 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__r
                                                                __half *kc, __half *vc,
                                                                const int32_t *__restrict__ lengths,
                                                                __half *__restrict__ out, int heads, int kvh,
-                                                               int max_pos, float scale, const RopeAppend ra) {
+                                                               int max_pos, float scale, const RopeAppend ra,
+                                                               const AttnSplit sp) {
   static_assert(HD == 64, "rows are 8 lanes x 8 halves");
   constexpr int kUnroll = 4;
-  extern __shared__ float sc[];  // [REP][max_pos]
-  __shared__ float sh[32];
-  __shared__ float outp[8][REP][HD];
+  constexpr int kWarps = 8;
+  constexpr int ST = 2 + HD;   // one softmax state: m, l, a[HD]
+  __shared__ float red[kWarps][REP][ST];
+  __shared__ int s_last;
   pdl_launch();
   pdl_wait();
-  const int b = blockIdx.x / kvh, g = blockIdx.x % kvh;
+  const int bg = blockIdx.x, b = bg / kvh, g = bg % kvh;
+  const int split = blockIdx.y, splits = gridDim.y;
   const int pos = lengths[b];
   const int len = min(pos + 1, max_pos);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int per = ((len + splits - 1) / splits + 15) & ~15;
+  const int j_begin = min(len, split * per), j_end = min(len, j_begin + per);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane >> 3, l8 = lane & 7;
   __half *kbase = kc + (int64_t(b) * kvh + g) * max_pos * HD;
   __half *vbase = vc + (int64_t(b) * kvh + g) * max_pos * HD;
   // RoPE staging v' = half(half(v cos) + half(rot(v) sin)), rot(v) = cat(-v[hd/2:], v[:hd/2]);
   // positions outside the table are left unrotated, as lb_rope does
   const bool rotate = ra.k_new != nullptr && pos >= 0 && pos < ra.table_rows;
-  if (ra.k_new != nullptr) {
-    if (threadIdx.x < HD / 2 && pos >= 0 && pos < max_pos) {
+  if (ra.k_new != nullptr && pos >= j_begin && pos < j_end) {
+    if (threadIdx.x < HD / 2) {
       const int i = threadIdx.x;
       const __half *kn = ra.k_new + int64_t(b) * ra.kv_stride + g * HD;
       const __half *vn = ra.v_new + int64_t(b) * ra.kv_stride + g * HD;
@@ -214,14 +241,28 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__r
 #pragma unroll
     for (int e = 0; e < 8; ++e) qv[r][e] = __half2float(qh[e]);
   }
-  // ---- scores -------------------------------------------------------------------------
-  for (int j0 = warp * 4 * kUnroll; j0 < len; j0 += nw * 4 * kUnroll) {
-    uint4 kv[kUnroll];
+  // ---- one pass: scores, running max / sum, p.V ------------------------------------
+  float m[REP], l[REP], a[REP][8];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[r][e] = 0.f;
+  }
+  for (int j0 = j_begin + warp * 4 * kUnroll; j0 < j_end; j0 += kWarps * 4 * kUnroll) {
+    uint4 kv[kUnroll], vv[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int j = j0 + u * 4 + sub;
-      kv[u] = j < len ? *reinterpret_cast<const uint4 *>(kbase + int64_t(j) * HD + l8 * 8) : make_uint4(0, 0, 0, 0);
+      kv[u] = j < j_end ? *reinterpret_cast<const uint4 *>(kbase + int64_t(j) * HD + l8 * 8) : make_uint4(0, 0, 0, 0);
     }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = j0 + u * 4 + sub;
+      vv[u] = j < j_end ? *reinterpret_cast<const uint4 *>(vbase + int64_t(j) * HD + l8 * 8) : make_uint4(0, 0, 0, 0);
+    }
+    float sc[kUnroll][REP];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int j = j0 + u * 4 + sub;
@@ -234,77 +275,102 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const __half *__r
         d += __shfl_xor_sync(0xffffffffu, d, 1);
         d += __shfl_xor_sync(0xffffffffu, d, 2);
         d += __shfl_xor_sync(0xffffffffu, d, 4);
-        if (l8 == 0 && j < len) sc[r * max_pos + j] = __half2float(__float2half_rn(__half2float(__float2half_rn(d)) * scale));
+        sc[u][r] = j < j_end ? __half2float(__float2half_rn(__half2float(__float2half_rn(d)) * scale)) : -INFINITY;
       }
     }
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float mx = m[r];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) mx = fmaxf(mx, sc[u][r]);
+      if (mx == -INFINITY) continue;           // no valid row in this step for this group
+      const float c = softmax_weight(m[r], mx);
+      l[r] *= c;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[r][e] *= c;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const float pj = softmax_weight(sc[u][r], mx);
+        l[r] += pj;
+        const __half *vh = reinterpret_cast<const __half *>(&vv[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[r][e] = fmaf(pj, __half2float(vh[e]), a[r][e]);
+      }
+      m[r] = mx;
+    }
   }
-  __syncthreads();
-  // ---- softmax in fp32, probabilities rounded to fp16 ----------------------------------
+  // ---- merge: the 4 row groups of the warp, then the warps, then the splits ----------
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
-    float mx = -INFINITY;
-    for (int j = threadIdx.x; j < len; j += blockDim.x) mx = fmaxf(mx, sc[r * max_pos + j]);
-    mx = block_max(mx, sh);
-    float sum = 0.f;
-    for (int j = threadIdx.x; j < len; j += blockDim.x) {
-      const float e = expf(sc[r * max_pos + j] - mx);
-      sc[r * max_pos + j] = e;
-      sum += e;
-    }
-    sum = block_sum(sum, sh);
-    for (int j = threadIdx.x; j < len; j += blockDim.x)
-      sc[r * max_pos + j] = __half2float(__float2half_rn(__fdiv_rn(sc[r * max_pos + j], sum)));
-  }
-  __syncthreads();
-  // ---- out = p . V: lane covers 8 dims of one row, 4 rows per warp per step ------------
-  float acc[REP][8];
 #pragma unroll
-  for (int r = 0; r < REP; ++r)
+    for (int o = 8; o <= 16; o <<= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[r], o);
+      const float lo = __shfl_xor_sync(0xffffffffu, l[r], o);
+      const float mn = fmaxf(m[r], mo);
+      const float ws = softmax_weight(m[r], mn), wo = softmax_weight(mo, mn);
+      l[r] = l[r] * ws + lo * wo;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
-  for (int j0 = warp * 4 * kUnroll; j0 < len; j0 += nw * 4 * kUnroll) {
-    uint4 vv[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int j = j0 + u * 4 + sub;
-      vv[u] = j < len ? *reinterpret_cast<const uint4 *>(vbase + int64_t(j) * HD + l8 * 8) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int j = j0 + u * 4 + sub;
-      if (j >= len) continue;
-      const __half *vh = reinterpret_cast<const __half *>(&vv[u]);
-#pragma unroll
-      for (int r = 0; r < REP; ++r) {
-        const float pj = sc[r * max_pos + j];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[r][e] = fmaf(pj, __half2float(vh[e]), acc[r][e]);
-      }
+      for (int e = 0; e < 8; ++e) a[r][e] = a[r][e] * ws + __shfl_xor_sync(0xffffffffu, a[r][e], o) * wo;
+      m[r] = mn;
     }
   }
-  // reduce the 4 row groups of the warp (lanes l8, l8+8, l8+16, l8+24), then across warps
-#pragma unroll
-  for (int r = 0; r < REP; ++r)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float v = acc[r][e];
-      v += __shfl_xor_sync(0xffffffffu, v, 8);
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      acc[r][e] = v;
-    }
   if (sub == 0) {
 #pragma unroll
-    for (int r = 0; r < REP; ++r)
+    for (int r = 0; r < REP; ++r) {
+      if (l8 == 0) {
+        red[warp][r][0] = m[r];
+        red[warp][r][1] = l[r];
+      }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) outp[warp][r][l8 * 8 + e] = acc[r][e];
+      for (int e = 0; e < 8; ++e) red[warp][r][2 + l8 * 8 + e] = a[r][e];
+    }
   }
   __syncthreads();
+  float *mine = splits > 1 ? sp.part + (int64_t(bg) * splits + split) * REP * ST : nullptr;
   for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
-    const int r = i / HD, dd = i % HD;
-    float s2 = 0.f;
-    for (int w = 0; w < nw; ++w) s2 += outp[w][r][dd];
-    out[int64_t(b) * heads * HD + (g * REP + r) * HD + dd] = __float2half_rn(s2);
+    const int r = i / HD, d = i % HD;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, red[w][r][0]);
+    float lt = 0.f, at = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = softmax_weight(red[w][r][0], mx);
+      lt += red[w][r][1] * wt;
+      at += red[w][r][2 + d] * wt;
+    }
+    if (splits == 1) {
+      out[int64_t(b) * heads * HD + (g * REP + r) * HD + d] = __float2half_rn(at / lt);
+    } else {
+      if (d == 0) {
+        mine[r * ST] = mx;
+        mine[r * ST + 1] = lt;
+      }
+      mine[r * ST + 2 + d] = at;
+    }
   }
+  if (splits == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(sp.counters + bg, 1) == splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float *all = sp.part + int64_t(bg) * splits * REP * ST;
+  for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
+    const int r = i / HD, d = i % HD;
+    float mx = -INFINITY;
+    for (int s2 = 0; s2 < splits; ++s2) mx = fmaxf(mx, __ldcg(all + (s2 * REP + r) * ST));
+    float lt = 0.f, at = 0.f;
+    for (int s2 = 0; s2 < splits; ++s2) {
+      const float *st = all + (s2 * REP + r) * ST;
+      const float wt = softmax_weight(__ldcg(st), mx);
+      lt += __ldcg(st + 1) * wt;
+      at += __ldcg(st + 2 + d) * wt;
+    }
+    out[int64_t(b) * heads * HD + (g * REP + r) * HD + d] = __float2half_rn(at / lt);
+  }
+  if (threadIdx.x == 0) sp.counters[bg] = 0;   // ready for the next call
 }
 
 // h = half(half(silu(float(gate))) * up)  (torch_npu_smollm.py:189-190)
@@ -549,50 +615,71 @@ cudaError_t launch_kv_append(const uint16_t *k, const uint16_t *v, int kv_stride
                   reinterpret_cast<__half *>(vc), lengths, batch, kvh, hd, max_pos);
 }
 
-size_t attention_smem(int heads, int kvh, int max_pos) { return size_t(heads / kvh) * max_pos * sizeof(float); }
+// Position splits per (sequence, kv head): enough CTAs for ~3 per SM, at least 256
+// positions per split, at most kMaxAttnSplits; none when the caller's workspace is too
+// small or the arrival counters would not fit.  LOWBIT_ATTN_SPLITS forces a count (tuning).
+constexpr int kMaxAttnSplits = 16;
+constexpr int kAttnCounters = 4094;   // the workspace's GEMV arrival counters, minus two reserved
+
+size_t attention_scratch_bytes(int batch, int heads, int splits) {
+  return size_t(batch) * heads * splits * (2 + 64) * sizeof(float);
+}
+
+int attention_splits(int batch, int kvh, int heads, int max_pos, size_t scratch_bytes) {
+  const int ctas = batch * kvh;
+  int s = std::min((444 + ctas - 1) / ctas, std::max(1, max_pos / 256));
+  if (const char *env = getenv("LOWBIT_ATTN_SPLITS")) s = atoi(env);
+  s = std::max(1, std::min(s, kMaxAttnSplits));
+  if (ctas > kAttnCounters) return 1;
+  while (s > 1 && attention_scratch_bytes(batch, heads, s) > scratch_bytes) --s;
+  return s;
+}
 
 template <int REP>
 static cudaError_t launch_attention_rep(const uint16_t *q, int q_stride, uint16_t *kc, uint16_t *vc,
                                         const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh,
-                                        int max_pos, float scale, size_t smem, const RopeAppend &ra, cudaStream_t st) {
-  auto kern = attention_decode_kernel<64, REP>;
-  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void *>(kern), int(smem));
-  if (e != cudaSuccess) return e;
-  return launch_k(kern, dim3(batch * kvh), dim3(256), smem, st, reinterpret_cast<const __half *>(q), q_stride,
-                  reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), lengths,
-                  reinterpret_cast<__half *>(out), heads, kvh, max_pos, scale, ra);
+                                        int max_pos, float scale, const RopeAppend &ra, int splits,
+                                        const AttnSplit &sp, cudaStream_t st) {
+  return launch_k(attention_decode_kernel<64, REP>, dim3(batch * kvh, splits), dim3(256), 0, st,
+                  reinterpret_cast<const __half *>(q), q_stride, reinterpret_cast<__half *>(kc),
+                  reinterpret_cast<__half *>(vc), lengths, reinterpret_cast<__half *>(out), heads, kvh, max_pos, scale,
+                  ra, sp);
 }
 
+// counters: the workspace's arrival counters; scratch / scratch_bytes: the rest of it.
 static cudaError_t launch_attention(const uint16_t *q, int q_stride, uint16_t *kc, uint16_t *vc,
                                     const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
-                                    int max_pos, float scale, const RopeAppend &ra, cudaStream_t st) {
+                                    int max_pos, float scale, const RopeAppend &ra, int *counters, void *scratch,
+                                    size_t scratch_bytes, cudaStream_t st) {
   if (hd != 64) return cudaErrorInvalidValue;
-  const size_t smem = attention_smem(heads, kvh, max_pos);
+  const int splits = counters && scratch ? attention_splits(batch, kvh, heads, max_pos, scratch_bytes) : 1;
+  AttnSplit sp;
+  sp.part = static_cast<float *>(scratch);
+  sp.counters = counters;
   switch (heads / kvh) {
-    case 1: return launch_attention_rep<1>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 2: return launch_attention_rep<2>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 3: return launch_attention_rep<3>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 4: return launch_attention_rep<4>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 5: return launch_attention_rep<5>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 6: return launch_attention_rep<6>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 7: return launch_attention_rep<7>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
-    case 8: return launch_attention_rep<8>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, smem, ra, st);
+#define LB_ATTN_CASE(R) \
+    case R: return launch_attention_rep<R>(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, max_pos, scale, ra, splits, sp, st);
+    LB_ATTN_CASE(1) LB_ATTN_CASE(2) LB_ATTN_CASE(3) LB_ATTN_CASE(4)
+    LB_ATTN_CASE(5) LB_ATTN_CASE(6) LB_ATTN_CASE(7) LB_ATTN_CASE(8)
+#undef LB_ATTN_CASE
     default: return cudaErrorInvalidValue;
   }
 }
 
 cudaError_t launch_attention_decode(const uint16_t *q, int q_stride, const uint16_t *kc, const uint16_t *vc,
                                     const int32_t *lengths, uint16_t *out, int batch, int heads, int kvh, int hd,
-                                    int max_pos, float scale, cudaStream_t st) {
+                                    int max_pos, float scale, int *counters, void *scratch, size_t scratch_bytes,
+                                    cudaStream_t st) {
   // without the prologue nothing writes the caches
   return launch_attention(q, q_stride, const_cast<uint16_t *>(kc), const_cast<uint16_t *>(vc), lengths, out, batch,
-                          heads, kvh, hd, max_pos, scale, RopeAppend{}, st);
+                          heads, kvh, hd, max_pos, scale, RopeAppend{}, counters, scratch, scratch_bytes, st);
 }
 
 cudaError_t launch_attention_decode_rope(const uint16_t *q, int q_stride, const uint16_t *k_new, const uint16_t *v_new,
                                          int kv_stride, const uint16_t *cos_t, const uint16_t *sin_t, int table_rows,
                                          uint16_t *kc, uint16_t *vc, const int32_t *lengths, uint16_t *out, int batch,
-                                         int heads, int kvh, int hd, int max_pos, float scale, cudaStream_t st) {
+                                         int heads, int kvh, int hd, int max_pos, float scale, int *counters,
+                                         void *scratch, size_t scratch_bytes, cudaStream_t st) {
   RopeAppend ra;
   ra.k_new = reinterpret_cast<const __half *>(k_new);
   ra.v_new = reinterpret_cast<const __half *>(v_new);
@@ -600,7 +687,8 @@ cudaError_t launch_attention_decode_rope(const uint16_t *q, int q_stride, const 
   ra.cos_t = reinterpret_cast<const __half *>(cos_t);
   ra.sin_t = reinterpret_cast<const __half *>(sin_t);
   ra.table_rows = table_rows;
-  return launch_attention(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, hd, max_pos, scale, ra, st);
+  return launch_attention(q, q_stride, kc, vc, lengths, out, batch, heads, kvh, hd, max_pos, scale, ra, counters,
+                          scratch, scratch_bytes, st);
 }
 
 cudaError_t launch_silu_mul(const uint16_t *gate, const uint16_t *up, int in_stride, uint16_t *out, int rows, int cols,

@@ -84,7 +84,10 @@ template <int BM> struct TcStages { static constexpr int S = BM >= 256 ? 4 : 6; 
 template <int FMT, int BM> struct TcLayout {
   static constexpr bool kDeq = FMT != LB_FMT_FP16;
   static constexpr int S = TcStages<BM>::S;          // TMA stages
-  static constexpr int SA = kDeq ? (BM >= 256 ? 3 : 2) : S;   // A buffers (fp16 weight tiles ride the TMA stages)
+  // A buffers (fp16 weight tiles ride the TMA stages).  An A buffer is reused only after
+  // the MMAs that read it complete, so with small activation tiles (short MMAs) the ring
+  // must be deep for the dequant warps to run ahead of the tensor cores.
+  static constexpr int SA = kDeq ? (BM >= 256 ? 3 : (BM >= 128 ? 4 : 6)) : S;
   static constexpr int A_BYTES = 128 * 128;          // 128 rows x 64 fp16
   static constexpr int B_BYTES = BM * 128;           // BM rows x 64 fp16
   static constexpr int C_BYTES = 128 * TcFmt<FMT>::CODE_BYTES;

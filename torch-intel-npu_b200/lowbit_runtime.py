@@ -40,7 +40,8 @@ SIGNATURES = {
     'lb_linear': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_path': ([_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _S, _P], _I),
     'lb_linear_select': ([_I, _I, _I, _I, _I, _I], _I),
-    'lb_attention_decode_rope': ([_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P], _I),
+    'lb_attention_decode_rope': ([_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _S, _P],
+                                 _I),
     'lb_linear_stacked': ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _S, _P], _I),
     'lb_rmsnorm_project': ([_P, _P, _P, _P, _P, _I, _I, _F, _P, _I, _P, _P], _I),
     'lb_silu_mul_project': ([_P, _P, _I, _P, _I, _I, _P, _I, _P, _P], _I),

@@ -184,9 +184,13 @@ class FrozenSmolLayer(torch.nn.Module):
         self._tp = tp_group
         self._row_corr = {}
         for name, (down, up) in (row_corrections or {}).items():
-            up64 = torch.zeros(up.shape[0], 64, dtype=torch.float16, device=self.device)
-            up64[:, :up.shape[1]] = up.to(self.device, torch.float16)
-            self._row_corr[name] = (down.to(self.device, torch.float16).contiguous(), up64)
+            # rank padded to 32 with zero factors: z keeps a 32-column row in the exchange buffer
+            r = down.shape[0]
+            down32 = torch.zeros(32, down.shape[1], dtype=torch.float16, device=self.device)
+            up32 = torch.zeros(up.shape[0], 32, dtype=torch.float16, device=self.device)
+            down32[:r] = down.to(self.device, torch.float16)
+            up32[:, :r] = up.to(self.device, torch.float16)
+            self._row_corr[name] = (down32, up32)
         self._owner = object()
         self.eval()
 
@@ -266,27 +270,32 @@ class FrozenSmolLayer(torch.nn.Module):
             return self._row_parallel(name, x)
         return rt.linear(x, p['fmt'], p['group'], p['n'], p['codes'], p['scales'], down=p['down'], up=p['up'], out=out)
 
-    def _row_parallel(self, name, x):
-        """Row-parallel projection: local partial y_r = half(x_r W_r^T) and z_r = x_r V_r^T,
-        one NCCL all-reduce (sum) over both, then y = half(y + half(z U^T)).  z and U are
-        zero-padded to 64 columns so the correction product runs on the linear kernels."""
+    def _row_parallel(self, name, x, z=None, buf=None):
+        """Row-parallel projection: the local partial y_r = half(x_r W_r^T) and the partial
+        correction projection z_r = half(x_r V_r^T) share one buffer, one NCCL all-reduce
+        (sum) combines both, then y = half(y + half(z U^T)) in one decode-GEMV launch (the
+        sum as its residual).  ``buf`` / ``z`` (a [M, 32] view at its end): the buffer and a
+        projection a producer kernel already wrote there (lb_silu_mul_project)."""
         import torch.distributed as dist
         p = self._proj[name]
         m, n = x.shape[0], p['n']
         corr = self._row_corr.get(name)
-        buf = torch.empty(m * n + (m * 64 if corr else 0), dtype=torch.float16, device=x.device)
+        if buf is None:
+            buf = torch.empty(m * n + (m * 32 if corr else 0), dtype=torch.float16, device=x.device)
         y = buf[:m * n].view(m, n)
         rt.linear(x, p['fmt'], p['group'], n, p['codes'], p['scales'], out=y)
         if corr is None:
             dist.all_reduce(buf, group=self._tp)
             return y
-        down, up64 = corr
-        r = down.shape[0]
-        z = buf[m * n:].view(m, 64)
-        z.zero_()
-        z[:, :r].copy_(rt.linear(x, 'fp16', x.shape[1], r, down.view(torch.uint8).reshape(-1), None))
+        down, up32 = corr
+        zv = buf[m * n:].view(m, 32)
+        if z is None:
+            rt.linear(x, 'fp16', x.shape[1], 32, down.view(torch.uint8).reshape(-1), None, out=zv)
         dist.all_reduce(buf, group=self._tp)
-        delta = rt.linear(z, 'fp16', 64, n, up64.view(torch.uint8).reshape(-1), None)
+        ucodes = up32.view(torch.uint8).reshape(-1)
+        if rt.linear_select('fp16', 32, m, n, 32) == 'gemv':
+            return rt.linear_stacked(zv, 'fp16', 32, n, ucodes, None, residual=y)
+        delta = rt.linear(zv, 'fp16', 32, n, ucodes, None)
         out = torch.empty_like(y)
         rt.check(rt.lib().lb_add(rt.ptr(y), rt.ptr(delta), rt.ptr(out), out.numel(), rt.stream_ptr(x.device)), 'lb_add')
         return out
@@ -454,10 +463,13 @@ class FrozenSmolLayer(torch.nn.Module):
         cos, sin = self._rope()
         attn = torch.empty(b, cfg.heads * cfg.head_dim, dtype=torch.float16, device=h.device)
         # RoPE of q / k at lengths[b], KV append and attention in one launch
+        # the stream's linear workspace also holds the attention's position-split scratch
+        ws = rt.Workspace.get(L.lb_attention_workspace_bytes(b, cfg.heads, self.max_positions), h.device)
         rt.check(L.lb_attention_decode_rope(rt.ptr(q), q.stride(0), rt.ptr(k), rt.ptr(v), k.stride(0), rt.ptr(cos),
                                             rt.ptr(sin), cos.shape[0], rt.ptr(k_cache), rt.ptr(v_cache), rt.ptr(lengths),
                                             rt.ptr(attn), b, cfg.heads, cfg.kv_heads, cfg.head_dim, self.max_positions,
-                                            1.0 / cfg.head_dim ** 0.5, st), 'lb_attention_decode_rope')
+                                            1.0 / cfg.head_dim ** 0.5, rt.ptr(ws), ws.numel(), st),
+                 'lb_attention_decode_rope')
         o = self.linear('self_attn.o_proj.weight', attn)
         h1 = torch.empty_like(h)
         gs = self._stack_for('gate_up', b)
@@ -475,6 +487,19 @@ class FrozenSmolLayer(torch.nn.Module):
         fused_down = self._tp is None and rt.linear_select(dp['fmt'], dp['group'], b, dp['n'], dp['k']) == 'gemv'
         rows, cols = gate.shape
         act = torch.empty(rows, cols, dtype=torch.float16, device=h.device)
+        if self._tp is not None:
+            # row-parallel down projection: SiLU-mul writes the partial z = act . V_r^T
+            # straight into the buffer the all-reduce sums
+            corr = self._row_corr.get('mlp.down_proj.weight')
+            buf = torch.empty(rows * dp['n'] + (rows * 32 if corr else 0), dtype=torch.float16, device=h.device)
+            zv = buf[rows * dp['n']:].view(rows, 32) if corr else None
+            rt.check(L.lb_silu_mul_project(rt.ptr(gate), rt.ptr(up), gate.stride(0), rt.ptr(act), rows, cols,
+                                           rt.ptr(corr[0] if corr else None), 32 if corr else 0, rt.ptr(zv), st),
+                     'lb_silu_mul_project')
+            down = self._row_parallel('mlp.down_proj.weight', act, z=zv, buf=buf)
+            out = torch.empty_like(h)
+            rt.check(L.lb_add(rt.ptr(h1), rt.ptr(down), rt.ptr(out), out.numel(), st), 'lb_add')
+            return out
         zd = None
         if fused_down and fuse_z and dp['down'] is not None:
             zd = torch.empty(rows, (dp['down'].shape[0] + 31) // 32 * 32, dtype=torch.float16, device=h.device)
