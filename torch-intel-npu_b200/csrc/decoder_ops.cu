@@ -527,9 +527,24 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __half *__restrict__
   const int64_t r = blockIdx.x;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = __half2float(logits[r * vocab + i]);
-    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  const __half *row = logits + r * vocab;
+  if ((vocab & 7) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    // 16-byte loads, every one in flight before the comparisons (ascending index within a
+    // thread, so ties keep the first index)
+    for (int c = threadIdx.x; c < vocab / 8; c += blockDim.x) {
+      const uint4 q = *reinterpret_cast<const uint4 *>(row + 8 * c);
+      const __half *h = reinterpret_cast<const __half *>(&q);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v = __half2float(h[e]);
+        if (v > best) { best = v; bi = 8 * c + e; }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+      const float v = __half2float(row[i]);
+      if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

@@ -84,10 +84,7 @@ template <int BM> struct TcStages { static constexpr int S = BM >= 256 ? 4 : 6; 
 template <int FMT, int BM> struct TcLayout {
   static constexpr bool kDeq = FMT != LB_FMT_FP16;
   static constexpr int S = TcStages<BM>::S;          // TMA stages
-  // A buffers (fp16 weight tiles ride the TMA stages).  An A buffer is reused only after
-  // the MMAs that read it complete, so with small activation tiles (short MMAs) the ring
-  // must be deep for the dequant warps to run ahead of the tensor cores.
-  static constexpr int SA = kDeq ? (BM >= 256 ? 3 : (BM >= 128 ? 4 : 6)) : S;
+  static constexpr int SA = kDeq ? (BM >= 256 ? 3 : 2) : S;   // A buffers (fp16 weight tiles ride the TMA stages)
   static constexpr int A_BYTES = 128 * 128;          // 128 rows x 64 fp16
   static constexpr int B_BYTES = BM * 128;           // BM rows x 64 fp16
   static constexpr int C_BYTES = 128 * TcFmt<FMT>::CODE_BYTES;
@@ -528,7 +525,10 @@ int tc_splits(int m, int n, int k) {
   const int stages = k / 64;
   int s = 1;
   if (tiles > 4096) return 1;   // the arrival counters live in a fixed 4096-entry region
-  while (tiles * s * 2 <= 2 * 148 && stages / (s * 2) >= 4) s *= 2;
+  // one wave (a CTA per SM) with at least 16 K stages per split: measured on B200 for
+  // 8192x2048 / 2048x8192 / 1536x576 at M = 16..128, a second wave or shorter splits cost
+  // more in partial sums than they gain
+  while (tiles * s * 2 <= 148 && stages / (s * 2) >= 16) s *= 2;
   return s;
 }
 

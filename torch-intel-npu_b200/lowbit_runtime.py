@@ -105,10 +105,25 @@ def _bind_fast_call(lib):
     _FAST_LINEAR = _lowbit_call.linear_path
 
 
+_RAW_STREAM = getattr(torch._C, '_cuda_getCurrentRawStream', None)
+
+
+def raw_stream(index):
+    """Raw handle of torch's current stream on CUDA device ``index``."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(index)
+    return torch.cuda.current_stream(torch.device('cuda', index)).cuda_stream
+
+
 def _current_stream(dev):
     """Raw handle of torch's current stream on CUDA device ``dev``."""
-    get = getattr(torch._C, '_cuda_getCurrentRawStream', None)
-    return get(dev.index) if get is not None else torch.cuda.current_stream(dev).cuda_stream
+    return raw_stream(dev.index)
+
+
+def linear_call():
+    """The callable that reaches lb_linear_path: the _lowbit_call module when built, else
+    the ctypes binding (same arguments: ints for pointers, None for null)."""
+    return _FAST_LINEAR if _FAST_LINEAR is not None else lib().lb_linear_path
 
 
 def lib():
@@ -275,6 +290,9 @@ def linear_workspace_bytes(fmt, group, m, n, k, rank):
 @functools.lru_cache(maxsize=4096)
 def _linear_ws_bytes(fmt_id, group, m, n, k, rank):
     return lib().lb_linear_workspace_bytes(fmt_id, group, m, n, k, rank)
+
+
+linear_ws_bytes_id = _linear_ws_bytes
 
 
 def _addr(t):

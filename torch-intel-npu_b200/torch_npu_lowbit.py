@@ -220,6 +220,16 @@ class QuantizedLinear(torch.nn.Module):
             down, up = correction.tensors()
             self._down, self._up = down.to(self._device), up.to(self._device)
         self._correction = correction
+        # per-call constants of the lb_linear_path call (forward's fast path)
+        n, k = weight.shape
+        self._n, self._k, self._dev_index = n, k, self._device.index
+        self._fmt_id = rt.LB_FMT[weight.format]
+        self._rank = 0 if self._down is None else self._down.shape[0]
+        self._ptrs = (self._codes.data_ptr(), self._scales.data_ptr(),
+                      None if self._down is None else self._down.data_ptr(),
+                      None if self._up is None else self._up.data_ptr())
+        self._bias_ptr = None if self._bias_dev is None else self._bias_dev.data_ptr()
+        self._ws = {}
 
     @property
     def weight(self):
@@ -250,12 +260,42 @@ class QuantizedLinear(torch.nn.Module):
                    compact_groups=compact_groups, activation_scale=activation_scale, correction=correction,
                    device=device)
 
-    def forward(self, x, *, out=None, path='auto'):
+    def _check_input(self, x):
         if (not isinstance(x, torch.Tensor) or x.dtype != torch.float16 or x.ndim != 2
                 or x.shape[1] != self.weight.shape[1]):
             raise ValueError('QuantizedLinear requires 2D FP16 activations with matching K')
         if x.device != self._device:
             raise ValueError(f'QuantizedLinear lives on {self._device}; got activations on {x.device}')
-        q = self._weight
-        return rt.linear(x.contiguous(), q.format, q.group_size, q.shape[0], self._codes, self._scales,
-                         down=self._down, up=self._up, bias=self._bias_dev, out=out, path=path)
+
+    def forward(self, x, *, out=None, path='auto'):
+        # fast checks first (a decode call is a few microseconds of GPU work); any mismatch
+        # takes the full validation, which raises the reference's error
+        if (type(x) is not torch.Tensor or x.dtype is not torch.float16 or x.dim() != 2 or x.shape[1] != self._k
+                or x.get_device() != self._dev_index):
+            self._check_input(x)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        m, n = x.shape[0], self._n
+        if out is None:
+            out = torch.empty(m, n, dtype=torch.float16, device=self._device)
+        elif (type(out) is not torch.Tensor or out.dtype is not torch.float16 or out.dim() != 2 or out.shape[0] != m
+              or out.shape[1] != n or out.get_device() != self._dev_index or not out.is_contiguous()):
+            raise ValueError('out must be a contiguous FP16 [M, N] tensor on the module device')
+        stream = rt.raw_stream(self._dev_index)
+        ws = self._ws.get((stream, m))
+        if ws is None:
+            if len(self._ws) > 64:
+                self._ws.clear()
+            ws = rt.Workspace.for_stream(rt.linear_ws_bytes_id(self._fmt_id, self.weight.group_size, m, n, self._k,
+                                                               self._rank), self._dev_index, stream)
+            if not torch.cuda.is_current_stream_capturing():
+                self._ws[(stream, m)] = ws
+        codes, scales, down, up = self._ptrs
+        status = rt.linear_call()(rt.PATH[path], self._fmt_id, self.weight.group_size, m, n, self._k, x.data_ptr(),
+                                  codes, scales, down, up, self._rank, self._bias_ptr, out.data_ptr(), ws.data_ptr(),
+                                  ws.numel(), stream)
+        if status != rt.OK:
+            rt.check(status, 'lb_linear')
+        if rt.CHECK_WAITS and not torch.cuda.is_current_stream_capturing():
+            rt.check(rt.lib().lb_workspace_check(ws.data_ptr(), ws.numel(), stream), 'lb_linear')
+        return out
