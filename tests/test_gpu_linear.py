@@ -339,3 +339,19 @@ def test_config0_w8_linear_matches_oracle(rt, m):
     expected = _oracle(x, (n, k), 'int8', group, data, scales, down=v, up=u)
     y = rt.linear(x.cuda(), 'int8', group, n, codes, sc, down=v.cuda(), up=u.cuda())
     _compare(y, expected, ('config0', m, rt.linear_select('int8', group, m, n, k, 32)))
+
+
+def test_forced_plan_the_shape_cannot_take_falls_back_consistently(rt, monkeypatch):
+    """A forced work split the shape cannot take (8 K-splitting warps over 5 K blocks) falls
+    back to one row group per warp; its grid covers exactly the rows, with the correction."""
+    monkeypatch.setenv('LOWBIT_GEMV_PLAN', '8,2,1')
+    n, k = 1536, 576
+    w, u, v = baseline_weight(n, k, seed=55)
+    group, data, scales = ref.quantize(w.numpy(), 'nf4', 64)
+    codes = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
+    sc = torch.frombuffer(bytearray(scales), dtype=torch.float16).cuda()
+    for m in (1, 3):
+        x = torch.randn(m, k, generator=torch.Generator().manual_seed(56 + m)).half()
+        expected = _oracle(x, (n, k), 'nf4', group, data, scales, down=v, up=u)
+        y = rt.linear(x.cuda(), 'nf4', group, n, codes, sc, down=v.cuda(), up=u.cuda(), path='gemv')
+        _compare(y, expected, ('fallback plan', m))

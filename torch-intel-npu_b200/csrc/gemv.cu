@@ -247,10 +247,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   if (p.up && (p.z || p.zv) && warp == kWarps - 1 && lane == 0 && blockIdx.y == 0) {
     // the correction factor rows of the CTA's epilogue (U is as constant as the codes):
     // in L2 by the time the main loop ends
-    const int rows = min(rows_cta, p.n - row0);
-    const __half *u0 = p.up + int64_t(row0) * p.rank;
-    const uint32_t bytes = uint32_t(rows) * p.rank * 2;
-    if ((bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(u0) & 15) == 0) prefetch_l2_bulk(u0, bytes);
+    const int rows = min(rows_cta, p.n - row0);   // <= 0 for a CTA past the last row
+    if (rows > 0) {
+      const __half *u0 = p.up + int64_t(row0) * p.rank;
+      const uint32_t bytes = uint32_t(rows) * uint32_t(p.rank) * 2u;
+      if ((bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(u0) & 15) == 0) prefetch_l2_bulk(u0, bytes);
+    }
   }
   if constexpr (FMT == LB_FMT_NF4) {
     fill_nf4_pair_lut<64>(lut);
@@ -825,7 +827,9 @@ static GemvPlan gemv_plan_search(int fmt, int m, int n, int k) {
   if (kblocks < 1 || groups < 1) return {1, 1, 1, 1, 1};
   int fwk = 0, frpw = 0, fsp = 0;
   if (const char *env = getenv("LOWBIT_GEMV_PLAN")) sscanf(env, "%d,%d,%d", &fwk, &frpw, &fsp);
-  GemvPlan best = {1, 1, 1, kblocks, groups};
+  // fallback (no candidate passed, e.g. a forced plan the shape cannot take): one row group
+  // per warp, 8 per CTA, the whole K range per warp
+  GemvPlan best = {1, 1, 1, kblocks, (groups + kWarps - 1) / kWarps};
   double best_cost = 1e30;
   for (int wk = 1; wk <= kWarps; wk *= 2) {
     for (int rpw = 1; rpw <= (m > 16 ? 1 : kMaxRowGroups); rpw *= 2) {
