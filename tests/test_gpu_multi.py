@@ -33,7 +33,11 @@ def _corrections(config, seed):
              for n, s in shapes.items() if len(s) == 2} for _ in range(config['num_hidden_layers'])]
 
 
-def _worker(rank, world, port, results):
+SMOL1700_2L = dict(CONFIG, hidden_size=2048, intermediate_size=8192, num_attention_heads=32, num_key_value_heads=32,
+                   vocab_size=49152, num_hidden_layers=2)
+
+
+def _worker(rank, world, port, results, config=CONFIG, graph=False, steps=16):
     import datetime
     import sys
     from pathlib import Path
@@ -46,27 +50,32 @@ def _worker(rank, world, port, results):
     torch.cuda.set_device(rank)
     dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device('cuda', rank))
-    lw, emb, norm = sm.random_smollm_weights(CONFIG, seed=0)
-    corr = _corrections(CONFIG, 1)
-    ids = torch.randint(0, 1024, (2, 12), generator=torch.Generator().manual_seed(2)).cuda()
-    tp = sp.build_tp_causal_lm(CONFIG, lw, emb, norm, mode='nf4a16', group_size=64, corrections=corr, rank=rank,
+    lw, emb, norm = sm.random_smollm_weights(config, seed=0)
+    corr = _corrections(config, 1)
+    ids = torch.randint(0, config['vocab_size'], (2, 12), generator=torch.Generator().manual_seed(2)).cuda()
+    tp = sp.build_tp_causal_lm(config, lw, emb, norm, mode='nf4a16', group_size=64, corrections=corr, rank=rank,
                                world=world, group=dist.group.WORLD, max_positions=64)
-    tokens, logits = tp.generate(ids, 16, graph=False, return_logits=True)
+    tokens, logits = tp.generate(ids, steps, graph=graph, return_logits=True)
     if rank == 0:
-        single = sp.build_tp_causal_lm(CONFIG, lw, emb, norm, mode='nf4a16', group_size=64, corrections=corr,
+        single = sp.build_tp_causal_lm(config, lw, emb, norm, mode='nf4a16', group_size=64, corrections=corr,
                                        rank=0, world=1, group=None, max_positions=64)
-        t1, l1 = single.generate(ids, 16, graph=False, return_logits=True)
-        err = max(float((a.float() - b.float()).norm() / b.float().norm()) for a, b in zip(logits, l1))
-        results['err'] = err
+        t1, l1 = single.generate(ids, steps, graph=graph, return_logits=True)
+        errs = [float((a.float() - b.float()).norm() / b.float().norm()) for a, b in zip(logits, l1)]
+        results['errs'] = errs
+        results['err'] = max(errs)
         results['same_tokens'] = bool(torch.equal(tokens, t1))
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs two GPUs')
-def test_tensor_parallel_decode_matches_single_gpu():
+@pytest.mark.parametrize('dims,graph', [('small', False), ('small', True), ('1.7b', True)])
+def test_tensor_parallel_decode_matches_single_gpu(dims, graph):
+    """Tensor parallel x2 against the same model on one GPU: eager and with the replayed
+    decode-step graph (NCCL all-reduces captured in it), at small and configs[4] dims."""
     manager = mp.Manager()
     results = manager.dict()
-    mp.spawn(_worker, args=(2, _port(), results), nprocs=2, join=True)
-    assert results['err'] < 5e-3
+    config = CONFIG if dims == 'small' else SMOL1700_2L
+    mp.spawn(_worker, args=(2, _port(), results, config, graph, 16 if dims == 'small' else 8), nprocs=2, join=True)
+    assert results['err'] < 5e-3, results['errs']
     assert results['same_tokens']

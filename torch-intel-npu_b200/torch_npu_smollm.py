@@ -35,6 +35,7 @@ from torch_npu_smollm_io import FrozenSmolIO
 _STACKS = {'qkv': ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight'),
            'gate_up': ('mlp.gate_proj.weight', 'mlp.up_proj.weight')}
 _FUSE_Z_ROWS = 16
+_ZP = 64   # columns of a row-parallel projection's z in the all-reduce buffer
 _PROJECTIONS = ('self_attn.q_proj.weight', 'self_attn.k_proj.weight', 'self_attn.v_proj.weight',
                 'self_attn.o_proj.weight', 'mlp.gate_proj.weight', 'mlp.up_proj.weight', 'mlp.down_proj.weight')
 _NORMS = ('input_layernorm.weight', 'post_attention_layernorm.weight')
@@ -184,13 +185,15 @@ class FrozenSmolLayer(torch.nn.Module):
         self._tp = tp_group
         self._row_corr = {}
         for name, (down, up) in (row_corrections or {}).items():
-            # rank padded to 32 with zero factors: z keeps a 32-column row in the exchange buffer
+            # rank padded to _ZP with zero factors: z keeps a _ZP-column row in the exchange
+            # buffer, and the z U^T product stays on the tensor-core path at prefill sizes
+            # (its K must be a multiple of 64)
             r = down.shape[0]
-            down32 = torch.zeros(32, down.shape[1], dtype=torch.float16, device=self.device)
-            up32 = torch.zeros(up.shape[0], 32, dtype=torch.float16, device=self.device)
-            down32[:r] = down.to(self.device, torch.float16)
-            up32[:, :r] = up.to(self.device, torch.float16)
-            self._row_corr[name] = (down32, up32)
+            downp = torch.zeros(_ZP, down.shape[1], dtype=torch.float16, device=self.device)
+            upp = torch.zeros(up.shape[0], _ZP, dtype=torch.float16, device=self.device)
+            downp[:r] = down.to(self.device, torch.float16)
+            upp[:, :r] = up.to(self.device, torch.float16)
+            self._row_corr[name] = (downp, upp)
         self._owner = object()
         self.eval()
 
@@ -273,29 +276,29 @@ class FrozenSmolLayer(torch.nn.Module):
     def _row_parallel(self, name, x, z=None, buf=None):
         """Row-parallel projection: the local partial y_r = half(x_r W_r^T) and the partial
         correction projection z_r = half(x_r V_r^T) share one buffer, one NCCL all-reduce
-        (sum) combines both, then y = half(y + half(z U^T)) in one decode-GEMV launch (the
-        sum as its residual).  ``buf`` / ``z`` (a [M, 32] view at its end): the buffer and a
-        projection a producer kernel already wrote there (lb_silu_mul_project)."""
+        (sum) combines both, then y = half(y + half(z U^T)) -- at decode sizes in one GEMV
+        launch (the sum as its residual).  ``buf`` / ``z`` (a [M, _ZP] view at its end): the
+        buffer and a projection a producer kernel already wrote there (lb_silu_mul_project)."""
         import torch.distributed as dist
         p = self._proj[name]
         m, n = x.shape[0], p['n']
         corr = self._row_corr.get(name)
         if buf is None:
-            buf = torch.empty(m * n + (m * 32 if corr else 0), dtype=torch.float16, device=x.device)
+            buf = torch.empty(m * n + (m * _ZP if corr else 0), dtype=torch.float16, device=x.device)
         y = buf[:m * n].view(m, n)
         rt.linear(x, p['fmt'], p['group'], n, p['codes'], p['scales'], out=y)
         if corr is None:
             dist.all_reduce(buf, group=self._tp)
             return y
-        down, up32 = corr
-        zv = buf[m * n:].view(m, 32)
+        down, upp = corr
+        zv = buf[m * n:].view(m, _ZP)
         if z is None:
-            rt.linear(x, 'fp16', x.shape[1], 32, down.view(torch.uint8).reshape(-1), None, out=zv)
+            rt.linear(x, 'fp16', x.shape[1], _ZP, down.view(torch.uint8).reshape(-1), None, out=zv)
         dist.all_reduce(buf, group=self._tp)
-        ucodes = up32.view(torch.uint8).reshape(-1)
-        if rt.linear_select('fp16', 32, m, n, 32) == 'gemv':
-            return rt.linear_stacked(zv, 'fp16', 32, n, ucodes, None, residual=y)
-        delta = rt.linear(zv, 'fp16', 32, n, ucodes, None)
+        ucodes = upp.view(torch.uint8).reshape(-1)
+        if rt.linear_select('fp16', _ZP, m, n, _ZP) == 'gemv':
+            return rt.linear_stacked(zv, 'fp16', _ZP, n, ucodes, None, residual=y)
+        delta = rt.linear(zv, 'fp16', _ZP, n, ucodes, None)
         out = torch.empty_like(y)
         rt.check(rt.lib().lb_add(rt.ptr(y), rt.ptr(delta), rt.ptr(out), out.numel(), rt.stream_ptr(x.device)), 'lb_add')
         return out
@@ -491,10 +494,10 @@ class FrozenSmolLayer(torch.nn.Module):
             # row-parallel down projection: SiLU-mul writes the partial z = act . V_r^T
             # straight into the buffer the all-reduce sums
             corr = self._row_corr.get('mlp.down_proj.weight')
-            buf = torch.empty(rows * dp['n'] + (rows * 32 if corr else 0), dtype=torch.float16, device=h.device)
-            zv = buf[rows * dp['n']:].view(rows, 32) if corr else None
+            buf = torch.empty(rows * dp['n'] + (rows * _ZP if corr else 0), dtype=torch.float16, device=h.device)
+            zv = buf[rows * dp['n']:].view(rows, _ZP) if corr else None
             rt.check(L.lb_silu_mul_project(rt.ptr(gate), rt.ptr(up), gate.stride(0), rt.ptr(act), rows, cols,
-                                           rt.ptr(corr[0] if corr else None), 32 if corr else 0, rt.ptr(zv), st),
+                                           rt.ptr(corr[0] if corr else None), _ZP if corr else 0, rt.ptr(zv), st),
                      'lb_silu_mul_project')
             down = self._row_parallel('mlp.down_proj.weight', act, z=zv, buf=buf)
             out = torch.empty_like(h)
