@@ -667,6 +667,10 @@ class SmolForCausalLM(torch.nn.Module):
         self.embedding = self.io.embedding
         self.final_norm = self.io.norm
         self._graphs = {}
+        # tensor-parallel stacks decode eagerly: NCCL all-reduces captured in the decode-step
+        # graph gave wrong logits (and, in one harness, never completed) on B200 + NCCL 2.28,
+        # while the eager path matches the single-GPU model
+        self._tensor_parallel = any(l._tp is not None for l in stack.layers)
 
     @classmethod
     def from_weights(cls, config, layer_weights, embedding, norm, **layer_options):
@@ -748,9 +752,10 @@ class SmolForCausalLM(torch.nn.Module):
         return logits
 
     def decode_step(self, b, graph=True):
-        """One greedy token for every sequence of the batch's session; returns fp16 logits."""
+        """One greedy token for every sequence of the batch's session; returns fp16 logits.
+        The step is a replayed CUDA graph, except for tensor-parallel stacks (eager)."""
         st = self.session(b)
-        if not graph:
+        if not graph or self._tensor_parallel:
             return self._decode_step(st)
         if st['graph'] is None:
             self._capture(st)
