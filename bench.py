@@ -149,8 +149,9 @@ def capture_steps(cells, stream):
 def launches_per_step(cells):
     """Kernel launches of one sweep step.  A corrected decode GEMV (M <= 16, rank <= 32)
     with >= 4 MiB of codes computes its z projection inside the same launch (the rule of
-    launch_gemv_fused_z in csrc/gemv.cu; the sweep's grids always fit the device at once);
-    otherwise the projection is a launch of its own."""
+    launch_gemv_fused_z in csrc/gemv.cu, for the one-row kernel of csrc/gemv1.cu as for the
+    general one; the sweep's grids always fit the device at once); otherwise the projection
+    is a launch of its own."""
     import lowbit_runtime as rt
     count = 0
     for c in cells:
@@ -200,7 +201,7 @@ def dominant_kernel_roofline(device, stream, peak_gbs):
         t = timed(lambda i: graph.replay(), 10, stream) / (10 * launches)
     per_launch = gemv_bytes(1, n, k, fmt, g, rank=0)
     achieved = per_launch / t / 1e9
-    return {'kernel': 'gemv_kernel<NF4> (8192x2048, group 64, M=1)', 'bound': 'hbm', 'achieved': round(achieved, 1),
+    return {'kernel': 'gemv1_kernel<NF4, group 64> (8192x2048, M=1)', 'bound': 'hbm', 'achieved': round(achieved, 1),
             'peak': peak_gbs, 'unit': 'GB/s', 'frac': round(achieved / peak_gbs, 4), 'launch_us': round(t * 1e6, 3),
             'bytes_per_launch': per_launch,
             'traffic': TRAFFIC_PER_LAUNCH.get(DOMINANT),
@@ -246,7 +247,7 @@ def prefill_roofline(device, stream, peak_tf, m):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel (mean of
 # the captured launches), from an ncu capture of `bench.py --profile dominant`.
-TRAFFIC_PER_LAUNCH = {DOMINANT: 8983552}
+TRAFFIC_PER_LAUNCH = {DOMINANT: 8973824}
 
 
 def cpu_reference_sweep(sample_cells, reps, cached=False):
@@ -775,7 +776,9 @@ def profile_case(which):
                    2176 cached positions, 570 MB of K/V), 4 launches;
       quantize  -- NF4 g64 quantize + pack of a 8192x2048 fp16 weight, 3 launches;
       decode    -- one greedy decode step of two configs[4] layers (+ head) at batch 32,
-                   replayed 3 times."""
+                   replayed 3 times;
+      decode360 -- one greedy decode step of two configs[3] layers (INT4, group 128 / 64,
+                   + head) at batch 64 over a 512-token prompt, replayed 3 times."""
     import lowbit_runtime as rt
     rt.require_cuda()
     fmt, g, n, k = DOMINANT
@@ -816,6 +819,13 @@ def profile_case(which):
         for _ in range(3):
             rt.quantize_pack(w, fmt, g)
         info.update(n=n, k=k, format=fmt, group=g)
+    elif which == 'decode360':
+        m = build_smollm('360m', 'w4a16', int4_groups(SMOL['360m']), torch.device('cuda'), 512 + 16, layers=2)
+        ids = torch.randint(0, m.config.vocab, (64, 512), generator=gen).cuda()
+        m.prefill_session(ids)
+        for _ in range(3):
+            m.decode_step(64)
+        info.update(layers=2, batch=64, prompt=512, launches_per_step=graph_kernel_nodes(m.session(64)['graph']))
     elif which == 'decode':
         m = build_smollm('1.7b', 'nf4a16', 64, torch.device('cuda'), 64 + 16, layers=2)
         ids = torch.randint(0, m.config.vocab, (32, 64), generator=gen).cuda()
@@ -839,7 +849,8 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decode', action='store_true')
     ap.add_argument('--quick-decode', action='store_true')
-    ap.add_argument('--profile', choices=['dominant', 'prefill', 'batched', 'attention', 'quantize', 'decode'],
+    ap.add_argument('--profile', choices=['dominant', 'prefill', 'batched', 'attention', 'quantize', 'decode',
+                                          'decode360'],
                     help='run a small fixed workload for an ncu capture and exit')
     args = ap.parse_args()
     if args.profile:

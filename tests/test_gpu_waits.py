@@ -1,7 +1,8 @@
 """Device-side bounded waits that run out are reported, and leave the library usable.
 
 The decode GEMV computes its rank-32 correction projection inside the same launch when
-the weight is large (>= 4 MB of codes, <= 16 activation rows): epilogue CTAs wait, with
+the weight is large (>= 4 MB of codes, <= 16 activation rows; one row of 4-bit codes runs
+the one-row kernel, 2 rows the general one, each with its own projection CTAs): CTAs wait, with
 a bound, for the CTAs that reduce the projection's K slices.  lb_test_wait_override
 shortens that bound to ~1 ms and makes the wait expect one arrival that no CTA makes, so
 the wait runs out for certain: the kernel records LB_ERR_TIMEOUT in the workspace status
@@ -26,18 +27,19 @@ def rt():
     lowbit_runtime.set_wait_checks(False)
 
 
-def _fused_case():
+def _fused_case(m):
     n, k = 8192, 2048
     gen = torch.Generator().manual_seed(77)
     w = (torch.randn(n, k, generator=gen) * 0.02).half()
     u = (torch.randn(n, 32, generator=gen) * 1e-3).half().cuda()
     v = (torch.randn(32, k, generator=gen) * 1e-3).half().cuda()
-    x = torch.randn(1, k, generator=gen).half().cuda()
+    x = torch.randn(m, k, generator=gen).half().cuda()
     return n, k, w, u, v, x
 
 
-def test_timed_out_wait_raises_and_the_next_call_is_clean(rt):
-    n, k, w, u, v, x = _fused_case()
+@pytest.mark.parametrize('m', [1, 2])
+def test_timed_out_wait_raises_and_the_next_call_is_clean(rt, m):
+    n, k, w, u, v, x = _fused_case(m)
     codes, sc = rt.quantize_pack(w.cuda(), 'nf4', 64)
     good = rt.linear(x, 'nf4', 64, n, codes, sc, down=v, up=u)
     torch.cuda.synchronize()
@@ -53,9 +55,10 @@ def test_timed_out_wait_raises_and_the_next_call_is_clean(rt):
         assert torch.equal(again, good)
 
 
-def test_timeout_is_found_by_a_later_device_check(rt):
+@pytest.mark.parametrize('m', [1, 2])
+def test_timeout_is_found_by_a_later_device_check(rt, m):
     """Without per-call checks (the CUDA-graph case), check_device_waits() reports it."""
-    n, k, w, u, v, x = _fused_case()
+    n, k, w, u, v, x = _fused_case(m)
     codes, sc = rt.quantize_pack(w.cuda(), 'nf4', 64)
     rt.lib().lb_test_wait_override(SHORT_WAIT, 1)
     rt.linear(x, 'nf4', 64, n, codes, sc, down=v, up=u)

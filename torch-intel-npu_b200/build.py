@@ -16,7 +16,7 @@ OUT = HERE / 'liblowbit.so'
 # CPython fast path for the per-call entry point (plain C over the C ABI, see csrc/pycall.c)
 PYCALL_OUT = HERE / ('_lowbit_call' + (sysconfig.get_config_var('EXT_SUFFIX') or '.so'))
 INCLUDE = HERE.parent / 'include'
-SOURCES = ['abi.cu', 'quantize.cu', 'gemv.cu', 'tc_gemm.cu', 'decoder_ops.cu', 'noalloc.cu']
+SOURCES = ['abi.cu', 'quantize.cu', 'gemv.cu', 'gemv1.cu', 'tc_gemm.cu', 'decoder_ops.cu', 'noalloc.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '-lineinfo', '-std=c++17',
          '-Xcompiler', '-fPIC', '-shared', '-cudart', 'shared', '--expt-relaxed-constexpr',

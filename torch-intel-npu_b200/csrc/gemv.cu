@@ -859,6 +859,13 @@ static GemvPlan gemv_plan_search(int fmt, int m, int n, int k) {
   return best;
 }
 
+bool gemv1_supported(int fmt, int group, int m, int n, int k, const void *x, const void *codes, const void *scales,
+                     const void *up, int rank);
+cudaError_t launch_gemv1(int fmt, int group, int n, int k, const uint16_t *x, const uint8_t *codes,
+                         const uint16_t *scales, const uint16_t *z, const uint16_t *down, const uint16_t *up, int rank,
+                         const uint16_t *bias, uint16_t *y, int *counters, float *zpart, int *err, cudaStream_t st);
+size_t gemv1_zpart_bytes();
+
 size_t gemv_workspace_bytes(int fmt, int m, int n, int k) {
   const GemvPlan pl = gemv_plan(fmt, m, n, k);
   if (pl.splits <= 1) return 0;
@@ -932,7 +939,7 @@ void set_wait_override(long long cycles, int missing) {
 }
 
 size_t gemv_fused_zpart_bytes(int m) {
-  return m <= kFuseZMaxRows ? size_t(kMaxZSlices) * m * 32 * sizeof(float) : 0;
+  return m <= kFuseZMaxRows ? std::max(size_t(kMaxZSlices) * m * 32 * sizeof(float), gemv1_zpart_bytes()) : 0;
 }
 
 template <int FMT, int NCOL, int GS = 0>
@@ -991,6 +998,10 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
                         const uint16_t *scales, const uint16_t *z, int zs, const uint16_t *up, int rank,
                         const uint16_t *bias, const uint16_t *resid, uint16_t *y, void *scratch, int *counters,
                         cudaStream_t st) {
+  // one activation row of 4-bit codes: the one-row kernel (csrc/gemv1.cu)
+  if (!resid && zs == 32 && rank <= 32 && gemv1_supported(fmt, group, m, n, k, x, codes, scales, z ? up : nullptr, rank))
+    return launch_gemv1(fmt, group, n, k, x, codes, scales, z, nullptr, z ? up : nullptr, rank, bias, y, nullptr, nullptr,
+                        nullptr, st);
   GemvParams p = {};
   p.m = m; p.n = n; p.k = k; p.group = fmt == LB_FMT_FP16 ? k : group;
   p.x = reinterpret_cast<const __half *>(x);
@@ -1043,6 +1054,17 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
                                 const uint16_t *bias, uint16_t *y, void *scratch, int *counters, float *zpart,
                                 int *err, cudaStream_t st, bool *fused) {
   *fused = false;
+  if (rank >= 1 && rank <= 32 && gemv1_supported(fmt, group, m, n, k, x, codes, scales, up, rank)) {
+    // the one-row kernel (csrc/gemv1.cu): the projection in the same launch from >= 4 MiB of
+    // codes (measured on B200: equal or faster there; below it the projection's own launch
+    // is faster), unless the grid could not be resident at once
+    if (int64_t(n) * k / 2 < kFuseZMinBytes || !zpart || !err) return cudaSuccess;
+    const cudaError_t e = launch_gemv1(fmt, group, n, k, x, codes, scales, nullptr, down, up, rank, bias, y, counters,
+                                       zpart, err, st);
+    if (e == cudaErrorNotSupported) return cudaSuccess;
+    *fused = true;
+    return e;
+  }
   const int bits = fmt == LB_FMT_INT8 ? 8 : (fmt == LB_FMT_FP16 ? 16 : 4);
   if (m > kFuseZMaxRows || rank < 1 || rank > 32 || !down || !zpart || !err ||
       int64_t(n) * k * bits / 8 < kFuseZMinBytes)
