@@ -513,14 +513,20 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   const int ktiles = zstride / 16;
   // even rank and a 4-byte aligned U: factor pairs are read as one word
   const bool u_pairs = (p.rank & 1) == 0 && (reinterpret_cast<uintptr_t>(p.up) & 3) == 0;
-  for (int rg = warp; rg < rows_cta / 16; rg += kWarps) {
+  // one (16-row group, 8-column group) tile per warp at a time: a CTA of 16 rows has 8
+  // column groups for its 8 warps at 64 activation rows
+  const int ncg = (p.m + 7) >> 3 < NCOL ? (p.m + 7) >> 3 : NCOL;
+  for (int job = warp; job < (rows_cta >> 4) * ncg; job += kWarps) {
+    const int rg = job / ncg, c = job - rg * ncg;
     const int rl0 = rg * 16;
-#pragma unroll
-    for (int c = 0; c < NCOL; ++c) {
-      if (8 * c >= p.m) break;
+    {
       const int mz = 8 * c + g;   // activation row of this lane's B column
       float d[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kt = 0; kt < ktiles; ++kt) {
+      // unrolled to the largest z width (128 columns): every k tile's U and z loads are
+      // issued together instead of one L2 round trip per tile
+#pragma unroll
+      for (int kt = 0; kt < 8; ++kt) {
+        if (kt >= ktiles) break;
         uint32_t ua[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -544,19 +550,40 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         }
         mma16816(d, ua, b0, b1);
       }
+      // the tile's per-row scale, bias and residual are all loaded before its first store
+      float rs[4], bi[4], re[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int mm = 8 * c + 2 * t + (i & 1), n = row0 + rl0 + g + 8 * (i >> 1);
+        const bool ok = n < p.n && mm < p.m;
+        rs[i] = (per_row_scale && ok) ? __half2float(p.scales[n]) : 1.f;
+        bi[i] = (p.bias && ok) ? __half2float(p.bias[n]) : 0.f;
+        re[i] = (p.resid && ok) ? __half2float(p.resid[int64_t(mm) * p.n + n]) : 0.f;
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int rl = rl0 + g + 8 * (i >> 1), mm = 8 * c + 2 * t + (i & 1), n = row0 + rl;
         if (n >= p.n || mm >= p.m) continue;
         float v = red[rl * LDC + mm];
-        if (per_row_scale) v *= __half2float(p.scales[n]);
+        if (per_row_scale) v *= rs[i];
         __half yq = __float2half_rn(v);
-        if (p.bias) yq = __float2half_rn(__half2float(yq) + __half2float(p.bias[n]));
+        if (p.bias) yq = __float2half_rn(__half2float(yq) + bi[i]);
         yq = __float2half_rn(__half2float(yq) + __half2float(__float2half_rn(d[i])));
-        if (p.resid) yq = __float2half_rn(__half2float(yq) + __half2float(p.resid[int64_t(mm) * p.n + n]));
-        p.y[int64_t(mm) * p.n + n] = yq;
+        if (p.resid) yq = __float2half_rn(__half2float(yq) + re[i]);
+        red[rl * LDC + mm] = __half2float(yq);   // the slot this lane alone read
       }
     }
+  }
+  // The finished tile goes out after the loop, in coalesced stores: with no global store
+  // inside it, nothing orders the next column group's U / z / residual loads behind the
+  // previous one's results (y could alias them as far as the compiler knows), so they
+  // overlap (measured on B200, at 64 activation rows storing in the loop serialised one L2
+  // round trip per column group and per residual element).
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < outs; idx += blockDim.x) {
+    const int mm = idx >> p.rows_shift, rl = idx & (rows_cta - 1), n = row0 + rl;
+    if (n >= p.n) continue;
+    p.y[int64_t(mm) * p.n + n] = __float2half_rn(red[rl * LDC + mm]);
   }
 }
 
