@@ -99,6 +99,9 @@ def test_path_selection():
     assert rt.linear_select('nf4', 64, 16, 8192, 2048) == 'gemv'
     assert rt.linear_select('nf4', 64, 64, 8192, 2048) == 'gemv'     # batched decode stays on the GEMV
     assert rt.linear_select('nf4', 64, 65, 8192, 2048) == 'tc'
+    assert rt.linear_select('fp16', 960, 64, 49152, 960) == 'tc'    # tied LM head at a decode batch
+    assert rt.linear_select('fp16', 960, 8, 49152, 960) == 'gemv'
+    assert rt.linear_select('fp16', 64, 64, 2048, 64) == 'gemv'      # narrow fp16 projections stay on the GEMV
     assert rt.linear_select('int8', 576, 128, 1536, 576) == 'tc'
     assert rt.linear_select('int4', 3, 1, 5, 9) == 'generic'      # odd shapes / groups
     assert rt.linear_select('nf4', 64, 128, 8192, 2048, 32) == 'tc'
