@@ -19,7 +19,7 @@
 // y = half(y + half(delta)), stored transposed to y[m, n].
 // Split-K (small M): each split writes fp32 partials to the caller's workspace and
 // finalize_kernel applies the same epilogue.
-// No TMA multicast is used anywhere.  Every mbarrier wait is bounded: on timeout the
+// Every TMA load is CTA-local (one CTA's own shared memory).  Every mbarrier wait is bounded: on timeout the
 // kernel records LB_ERR_TIMEOUT in the workspace flag, drains and returns.
 #include <cuda.h>
 #include <cstdlib>
