@@ -69,11 +69,12 @@ def _worker(rank, world, port, results, config=CONFIG, graph=False, steps=16):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs two GPUs')
-@pytest.mark.parametrize('dims,graph', [('small', False), ('1.7b', False)])
+@pytest.mark.parametrize('dims,graph', [('small', False), ('1.7b', False), ('small', True), ('1.7b', True)])
 def test_tensor_parallel_decode_matches_single_gpu(dims, graph):
-    """Tensor parallel x2 against the same model on one GPU, at small and configs[4] dims.
-    Tensor-parallel decode runs eagerly (SmolForCausalLM does not capture NCCL all-reduces in
-    its decode-step graph), so graph=False is the path the benchmark times."""
+    """Tensor parallel x2 against the same model on one GPU, at small and configs[4] dims,
+    eager and graphed.  A graphed tensor-parallel step is CUDA graphs split at the NCCL
+    all-reduces, which run eagerly between them (the path the benchmark times); the
+    single-GPU model it is compared with replays one graph per step."""
     manager = mp.Manager()
     results = manager.dict()
     config = CONFIG if dims == 'small' else SMOL1700_2L

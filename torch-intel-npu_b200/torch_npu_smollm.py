@@ -42,6 +42,77 @@ _NORMS = ('input_layernorm.weight', 'post_attention_layernorm.weight')
 _WEIGHT_FORMATS = {'fp16': None, 'w8a16': 'int8', 'w4a16': 'int4', 'nf4a16': 'nf4'}
 
 
+class _PiecewiseGraph:
+    """A decode step of a tensor-parallel stack as CUDA graphs split at its all-reduces.
+
+    While recording, the step runs once on a side stream under capture; each all-reduce
+    (``all_reduce``) ends the graph being captured, is kept as an eager step on its buffer,
+    and a new graph begins.  The graphs share one memory pool and ``replay`` runs them in
+    capture order, so a buffer allocated in one graph and summed before the next keeps its
+    address.  The NCCL calls themselves are never captured."""
+
+    active = None   # the recorder in use while a step is being captured
+
+    def __init__(self, device):
+        self.device = device
+        self.pool = torch.cuda.graph_pool_handle()
+        self.steps = []
+        self.graph = None
+
+    def _begin(self):
+        self.graph = torch.cuda.CUDAGraph(keep_graph=True)   # kept for launch counting
+        # thread-local: the process group's watchdog thread keeps querying its events
+        self.graph.capture_begin(pool=self.pool, capture_error_mode='thread_local')
+
+    def _end(self):
+        self.graph.capture_end()
+        self.steps.append(('graph', self.graph))
+        self.graph = None
+
+    def record(self, fn):
+        """Capture ``fn()`` (the decode step) on the current stream; returns its result."""
+        _PiecewiseGraph.active = self
+        try:
+            self._begin()
+            out = fn()
+            self._end()
+        finally:
+            _PiecewiseGraph.active = None
+            if self.graph is not None:   # an error inside a capture: close it before raising
+                try:
+                    self.graph.capture_end()
+                except RuntimeError:
+                    pass
+                self.graph = None
+        return out
+
+    def all_reduce(self, buf, group):
+        self._end()
+        self.steps.append(('all_reduce', buf, group))
+        self._begin()
+
+    def replay(self):
+        import torch.distributed as dist
+        for step in self.steps:
+            if step[0] == 'graph':
+                step[1].replay()
+            else:
+                dist.all_reduce(step[1], group=step[2])
+
+    def graphs(self):
+        return [s[1] for s in self.steps if s[0] == 'graph']
+
+
+def _all_reduce(buf, group):
+    """Sum ``buf`` over the tensor-parallel group, or record it as a split point of the
+    piecewise decode graph being captured."""
+    if _PiecewiseGraph.active is not None:
+        _PiecewiseGraph.active.all_reduce(buf, group)
+        return
+    import torch.distributed as dist
+    dist.all_reduce(buf, group=group)
+
+
 def _projection_policy(mode, names):
     """torch_npu_smollm.py:31-37."""
     if (type(names) is not tuple or any(type(name) is not str for name in names)
@@ -279,7 +350,6 @@ class FrozenSmolLayer(torch.nn.Module):
         (sum) combines both, then y = half(y + half(z U^T)) -- at decode sizes in one GEMV
         launch (the sum as its residual).  ``buf`` / ``z`` (a [M, _ZP] view at its end): the
         buffer and a projection a producer kernel already wrote there (lb_silu_mul_project)."""
-        import torch.distributed as dist
         p = self._proj[name]
         m, n = x.shape[0], p['n']
         corr = self._row_corr.get(name)
@@ -288,13 +358,13 @@ class FrozenSmolLayer(torch.nn.Module):
         y = buf[:m * n].view(m, n)
         rt.linear(x, p['fmt'], p['group'], n, p['codes'], p['scales'], out=y)
         if corr is None:
-            dist.all_reduce(buf, group=self._tp)
+            _all_reduce(buf, self._tp)
             return y
         down, upp = corr
         zv = buf[m * n:].view(m, _ZP)
         if z is None:
             rt.linear(x, 'fp16', x.shape[1], _ZP, down.view(torch.uint8).reshape(-1), None, out=zv)
-        dist.all_reduce(buf, group=self._tp)
+        _all_reduce(buf, self._tp)
         ucodes = upp.view(torch.uint8).reshape(-1)
         if rt.linear_select('fp16', _ZP, m, n, _ZP) == 'gemv':
             return rt.linear_stacked(zv, 'fp16', _ZP, n, ucodes, None, residual=y)
@@ -667,9 +737,9 @@ class SmolForCausalLM(torch.nn.Module):
         self.embedding = self.io.embedding
         self.final_norm = self.io.norm
         self._graphs = {}
-        # tensor-parallel stacks decode eagerly: NCCL all-reduces captured in the decode-step
-        # graph gave wrong logits (and, in one harness, never completed) on B200 + NCCL 2.28,
-        # while the eager path matches the single-GPU model
+        # tensor-parallel stacks keep their all-reduces out of the captured graphs: NCCL
+        # all-reduces captured in the decode-step graph gave wrong logits (and, in one harness,
+        # never completed) on B200 + NCCL 2.28, so the step is graphs split at the all-reduces
         self._tensor_parallel = any(l._tp is not None for l in stack.layers)
 
     @classmethod
@@ -753,16 +823,22 @@ class SmolForCausalLM(torch.nn.Module):
 
     def decode_step(self, b, graph=True):
         """One greedy token for every sequence of the batch's session; returns fp16 logits.
-        The step is a replayed CUDA graph, except for tensor-parallel stacks (eager)."""
+        The step is a replayed CUDA graph; for a tensor-parallel stack, a chain of graphs split
+        at its all-reduces, which run eagerly between them (_PiecewiseGraph)."""
         st = self.session(b)
-        if not graph or self._tensor_parallel:
+        if not graph:
             return self._decode_step(st)
+        if self._tensor_parallel:
+            if st.get('piecewise') is None:
+                self._capture(st, piecewise=True)
+            st['piecewise'].replay()
+            return st['logits']
         if st['graph'] is None:
             self._capture(st)
         st['graph'].replay()
         return st['logits']
 
-    def _capture(self, st):
+    def _capture(self, st, piecewise=False):
         stream = torch.cuda.current_stream(self.device)
         saved, ids = st['lengths'].clone(), st['ids'].clone()
         side = torch.cuda.Stream(self.device)
@@ -771,11 +847,26 @@ class SmolForCausalLM(torch.nn.Module):
             self._decode_step(st)            # warm-up: sizes workspaces outside capture
             st['lengths'].copy_(saved)
             st['ids'].copy_(ids)
-            g = torch.cuda.CUDAGraph(keep_graph=True)   # kept for launch counting (cudaGraphGetNodes)
-            with torch.cuda.graph(g, stream=side):
-                st['logits'] = self._decode_step(st)
+            if piecewise:
+                side.synchronize()
+                rec = _PiecewiseGraph(self.device)
+                st['logits'] = rec.record(lambda: self._decode_step(st))
+            else:
+                g = torch.cuda.CUDAGraph(keep_graph=True)   # kept for launch counting (cudaGraphGetNodes)
+                with torch.cuda.graph(g, stream=side):
+                    st['logits'] = self._decode_step(st)
         stream.wait_stream(side)
-        st['graph'] = g
+        if piecewise:
+            st['piecewise'] = rec
+        else:
+            st['graph'] = g
+
+    def release_graphs(self):
+        """Drop every captured decode graph (before destroying a tensor-parallel process group)."""
+        for st in self._graphs.values():
+            st['graph'] = None
+            st['piecewise'] = None
+            st['logits'] = None
 
     def generate(self, ids, steps, *, graph=True, return_logits=False):
         """Greedy decoding: prefill ``ids`` [B, S] (device int64), then ``steps`` tokens.
