@@ -1085,7 +1085,11 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
     // the one-row kernel (csrc/gemv1.cu): the projection in the same launch from >= 4 MiB of
     // codes (measured on B200: equal or faster there; below it the projection's own launch
     // is faster), unless the grid could not be resident at once
-    if (int64_t(n) * k / 2 < kFuseZMinBytes || !zpart || !err) return cudaSuccess;
+    static const int64_t g1_min = [] {   // LOWBIT_G1_FUSE_MIN: the threshold in code bytes (comparison)
+      const char *v = getenv("LOWBIT_G1_FUSE_MIN");
+      return v ? int64_t(atoll(v)) : kFuseZMinBytes;
+    }();
+    if (int64_t(n) * k / 2 < g1_min || !zpart || !err) return cudaSuccess;
     const cudaError_t e = launch_gemv1(fmt, group, n, k, x, codes, scales, nullptr, down, up, rank, bias, y, counters,
                                        zpart, err, st);
     if (e == cudaErrorNotSupported) return cudaSuccess;

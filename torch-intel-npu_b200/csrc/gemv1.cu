@@ -46,6 +46,7 @@ constexpr int kG1MaxRowGroups = 1 << 16;   // shared pieces per CTA stay small (
 constexpr int kG1Counters = 4096;          // arrival counters in the workspace header
 constexpr int kG1Done = kG1Counters - 3;   // in-launch projection: CTAs done with the slices
 constexpr int kG1ZArrive = kG1Counters - 2;   //   and slices arrived
+constexpr int kG1ZWords = kG1Done - 32;       //   and the projection's 32 words (0 = not written)
 constexpr int kG1MaxSlices = 32;
 
 struct Gemv1Params {
@@ -65,7 +66,7 @@ struct Gemv1Params {
   int rank;
   int zx;                // CTAs computing z slices (first in the grid; 0 without zv)
   float *zpart;          // [zx][32] slice partials (fp32)
-  int *counters;         // kG1Done, kG1ZArrive of the workspace counters (zero between calls)
+  int *counters;         // the workspace counters: kG1ZWords.., kG1Done, kG1ZArrive (zero between calls)
   int *err;              // status word (LB_ERR_TIMEOUT)
   long long wait_cycles;
   int z_extra;           // test hook: slice arrivals waited for beyond zx (0 in use)
@@ -75,6 +76,14 @@ __device__ __forceinline__ int g1_ld_acquire(const int *p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ uint32_t g1_ld_relaxed(const int *p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void g1_st_relaxed(int *p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ int g1_atom_add_acq_rel(int *p, int v) {
   int old;
@@ -106,24 +115,62 @@ __device__ __forceinline__ uint32_t g1_lds_imm(uint32_t a) {
 
 // One K slice of z^T = V x^T (slice blockIdx.x of zx): warp w < 8 owns ranks 4w .. 4w + 3,
 // lane l the slice's 16-byte chunks l, l + 32, ...; fp16 products exact, fp32 sums.  Every
-// writer fences its partials before the CTA counts the slice arrived.
-__device__ void g1_z_slice(const Gemv1Params &p) {
+// writer fences its partials before the CTA counts the slice arrived.  The slice that
+// arrives last sums the partials in slice order (g1_sum_slices), rounds each to half and
+// publishes z[r] as the word ~bits(float(z[r])) in counters[kG1ZWords + r]: a word is 0 until
+// written (the header is zero between calls) and never 0 once written (0xffffffff is not the
+// float of a half).  It then counts itself done with the main CTAs, so the words it stored
+// precede the last CTA's reset.
+__device__ __forceinline__ uint32_t g1_sum_slices(const Gemv1Params &p, int r) {
+  float v[kG1MaxSlices];   // every partial in flight at once (one L2 round trip), then summed in order
+#pragma unroll
+  for (int sl = 0; sl < kG1MaxSlices; ++sl) v[sl] = sl < p.zx ? __ldcg(p.zpart + sl * 32 + r) : 0.f;
+  float s = 0.f;
+#pragma unroll
+  for (int sl = 0; sl < kG1MaxSlices; ++sl)
+    if (sl < p.zx) s += v[sl];
+  const float z = r < p.rank ? __half2float(__float2half_rn(s)) : 0.f;
+  return ~__float_as_uint(z);
+}
+
+__device__ __forceinline__ void g1_release_z(const Gemv1Params &p);
+
+// s_last: one int of the slice CTA's dynamic shared memory (a static __shared__ variable
+// would move the dynamic base that the NF4 table's immediate-offset loads rely on).
+__device__ void g1_z_slice(const Gemv1Params &p, int *s_last) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunks = p.k >> 3;
   const int c0 = int(int64_t(blockIdx.x) * chunks / p.zx), c1 = int(int64_t(blockIdx.x + 1) * chunks / p.zx);
   if (warp < 8) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = c0 + lane; c < c1; c += 32) {
-      const uint4 xv = *reinterpret_cast<const uint4 *>(p.x + 8 * int64_t(c));
+    // two chunks per lane and step, all their loads issued before the first product (the
+    // chunks still reach each sum in the order c, c + 32, c + 64, ...)
+    for (int c = c0 + lane; c < c1; c += 64) {
+      const bool two = c + 32 < c1;
+      const uint4 zero = make_uint4(0, 0, 0, 0);
+      const uint4 xa = *reinterpret_cast<const uint4 *>(p.x + 8 * int64_t(c));
+      const uint4 xb = two ? *reinterpret_cast<const uint4 *>(p.x + 8 * int64_t(c + 32)) : zero;
+      uint4 va[4], vb[4];
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int rr = 4 * warp + r;
-        if (rr >= p.rank) break;
-        const uint4 v = ldg_nc_v4(p.zv + int64_t(rr) * p.k + 8 * int64_t(c));
-        fma2_f16_f32(acc[r], v.x, xv.x);
-        fma2_f16_f32(acc[r], v.y, xv.y);
-        fma2_f16_f32(acc[r], v.z, xv.z);
-        fma2_f16_f32(acc[r], v.w, xv.w);
+        const __half *vr = p.zv + int64_t(rr) * p.k + 8 * int64_t(c);
+        va[r] = rr < p.rank ? ldg_nc_v4(vr) : zero;
+        vb[r] = rr < p.rank && two ? ldg_nc_v4(vr + 256) : zero;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if (4 * warp + r >= p.rank) break;
+        fma2_f16_f32(acc[r], va[r].x, xa.x);
+        fma2_f16_f32(acc[r], va[r].y, xa.y);
+        fma2_f16_f32(acc[r], va[r].z, xa.z);
+        fma2_f16_f32(acc[r], va[r].w, xa.w);
+        if (two) {
+          fma2_f16_f32(acc[r], vb[r].x, xb.x);
+          fma2_f16_f32(acc[r], vb[r].y, xb.y);
+          fma2_f16_f32(acc[r], vb[r].z, xb.z);
+          fma2_f16_f32(acc[r], vb[r].w, xb.w);
+        }
       }
     }
 #pragma unroll
@@ -134,39 +181,57 @@ __device__ void g1_z_slice(const Gemv1Params &p) {
     if (lane == 0) __threadfence();   // this writer's partials reach L2 before the arrival
   }
   __syncthreads();
-  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.counters + kG1ZArrive) : "memory");
+  if (threadIdx.x == 0) *s_last = g1_atom_add_acq_rel(p.counters + kG1ZArrive, 1) == p.zx + p.z_extra - 1;
+  __syncthreads();
+  if (*s_last && threadIdx.x < 32) {
+    g1_st_relaxed(p.counters + kG1ZWords + threadIdx.x, g1_sum_slices(p, threadIdx.x));
+    __threadfence();   // every lane's word before the done count below
+    __syncwarp();
+    if (threadIdx.x == 0) g1_release_z(p);
+  }
 }
 
-// The projection, once per main CTA: wait (bounded) until every slice arrived, then
-// z[r] = half(sum of the slices in slice order) into zs[32] (fp32 values of the halves);
-// the CTA counts itself done and the last main CTA leaves both counters at zero.
-__device__ __forceinline__ void g1_collect_z(const Gemv1Params &p, float *zs, float *red) {
-  if (threadIdx.x == 0) {
-    const int want = p.zx + p.z_extra;
-    if (g1_ld_acquire(p.counters + kG1ZArrive) < want) {
-      const long long t0 = clock64();
-      while (g1_ld_acquire(p.counters + kG1ZArrive) < want)
-        if (clock64() - t0 > p.wait_cycles) { atomicExch(p.err, LB_ERR_TIMEOUT); break; }
-    }
-  }
-  __syncthreads();
-  const int r = threadIdx.x & 31, grp = threadIdx.x >> 5;
-  if (grp < 8) {   // 8 groups of slices in parallel, then the groups in order (deterministic)
-    float s = 0.f;
-    for (int sl = grp; sl < p.zx; sl += 8) s += __ldcg(p.zpart + sl * 32 + r);
-    red[grp * 32 + r] = s;
-  }
-  __syncthreads();
+// The projection, once per main CTA, by warp 0 into zs[32] (fp32 values of the halves):
+// the published words when they are all there, else -- once every slice has arrived -- the
+// same sums from the partials (same order, so the same bits).  The wait is bounded: on
+// timeout the status word says so and the projection counts 0.
+__device__ __forceinline__ void g1_collect_z(const Gemv1Params &p, float *zs) {
   if (threadIdx.x < 32) {
-    float s = 0.f;
-#pragma unroll
-    for (int gg = 0; gg < 8; ++gg) s += red[gg * 32 + threadIdx.x];
-    zs[threadIdx.x] = int(threadIdx.x) < p.rank ? __half2float(__float2half_rn(s)) : 0.f;
+    const int lane = threadIdx.x;
+    const int want = p.zx + p.z_extra;
+    uint32_t w = g1_ld_relaxed(p.counters + kG1ZWords + lane);
+    if (!__all_sync(0xffffffffu, w != 0u)) {
+      const long long t0 = clock64();
+      while (true) {
+        // all slices in, as seen by every lane's own acquire (a warp-uniform decision)
+        if (__all_sync(0xffffffffu, g1_ld_acquire(p.counters + kG1ZArrive) >= want)) {
+          w = g1_sum_slices(p, lane);
+          break;
+        }
+        w = g1_ld_relaxed(p.counters + kG1ZWords + lane);
+        if (__all_sync(0xffffffffu, w != 0u)) break;
+        if (__any_sync(0xffffffffu, clock64() - t0 > p.wait_cycles)) {
+          if (lane == 0) atomicExch(p.err, LB_ERR_TIMEOUT);
+          w = 0u;
+          break;
+        }
+      }
+    }
+    zs[lane] = w != 0u ? __uint_as_float(~w) : 0.f;
   }
-  __syncthreads();   // every thread of the CTA has read the slices
-  if (threadIdx.x == 0 && g1_atom_add_acq_rel(p.counters + kG1Done, 1) == int(gridDim.x) - p.zx - 1) {
-    p.counters[kG1Done] = 0;
+  __syncthreads();
+}
+
+// One count per main CTA (after its projection was read) and one from the publishing slice
+// (after its words were stored; none when the test hook withholds it): the last leaves the
+// words and both counters at zero for the next call.
+__device__ __forceinline__ void g1_release_z(const Gemv1Params &p) {
+  const int total = int(gridDim.x) - p.zx + (p.z_extra == 0 ? 1 : 0);
+  if (g1_atom_add_acq_rel(p.counters + kG1Done, 1) == total - 1) {
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) p.counters[kG1ZWords + r] = 0;
     p.counters[kG1ZArrive] = 0;
+    p.counters[kG1Done] = 0;
   }
 }
 
@@ -382,7 +447,7 @@ __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params
   extern __shared__ __align__(16) uint8_t g1_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // shared layout: [NF4 table] [x staged, k halves] [INT4: per-group offset sums, k / GS
-  // floats] [row-group pieces, rmax x W x 16 floats] [the projection, 32 floats] [8 x 32 slice sums]
+  // floats] [row-group pieces, rmax x W x 16 floats] [the projection, 32 floats]
   float *s_c = reinterpret_cast<float *>(g1_smem + kLutBytes + 2 * p.k);
   float *part = s_c + (kNF4 ? 0 : p.k / GS);
 
@@ -394,7 +459,7 @@ __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params
     }
     pdl_launch();
     pdl_wait();
-    g1_z_slice(p);
+    g1_z_slice(p, reinterpret_cast<int *>(g1_smem));
     return;
   }
 
@@ -483,9 +548,11 @@ __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params
   const bool corr = p.up && (p.z || p.zv);
   uint4 u[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
   if (corr && p.rank == 32 && warp < nr) g1_load_u(p, rc0 + warp, u);
-  float *zs = part + p.rmax * W * 16;   // [32] the projection, then [8][32] slice sums
+  float *zs = part + p.rmax * W * 16;   // [32] the projection
   if (p.zv) {
-    g1_collect_z(p, zs, zs + 32);
+    g1_collect_z(p, zs);
+    // the CTA's done count from the last warp, off the path of the epilogues of warps < nr
+    if (threadIdx.x == 32 * (W - 1)) g1_release_z(p);
   } else if (corr) {
     if (threadIdx.x < 32) zs[threadIdx.x] = int(threadIdx.x) < p.rank ? __half2float(p.z[threadIdx.x]) : 0.f;
     __syncthreads();
@@ -572,7 +639,7 @@ size_t gemv1_zpart_bytes() { return size_t(kG1MaxSlices) * 32 * sizeof(float); }
 template <int FMT, int GS, int W>
 static size_t g1_smem_bytes(int k, int rmax) {
   return size_t(FMT == LB_FMT_NF4 ? kG1Lut : 0) + 2 * size_t(k) + (FMT == LB_FMT_NF4 ? 0 : size_t(k / GS) * 4) +
-         size_t(rmax) * W * 16 * 4 + 9 * 32 * 4;
+         size_t(rmax) * W * 16 * 4 + 32 * 4;
 }
 
 template <int FMT, int GS, int W>
