@@ -865,6 +865,58 @@ def profile_case(which):
     return 0
 
 
+def cells_report(steps=5):
+    """Per-cell device time of the sweep (``--cells``): each cell alone, with and without its
+    rank-32 correction, over enough weight replicas to stream ~300 MB per pass (> 2x L2),
+    one graph of back-to-back lb_linear calls per case; then the sweep graph itself with and
+    without the corrections.  CUDA events on the launching stream; one JSON line."""
+    import lowbit_runtime as rt
+    rt.require_cuda()
+    device = torch.device('cuda')
+    stream = torch.cuda.Stream()
+    cells = make_cells(device)
+    gen = torch.Generator(device='cpu').manual_seed(1)
+
+    def graph_us(calls, per_replay):
+        with torch.cuda.stream(stream):
+            for f in calls:   # workspaces sized outside the capture
+                f()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for f in calls:
+                    f()
+            for _ in range(3):
+                g.replay()
+            t = timed(lambda i: g.replay(), steps, stream)
+        return t / steps / per_replay * 1e6
+
+    def call(c, codes, scales, corr):
+        kw = dict(down=c['v'], up=c['u']) if corr else {}
+        return lambda: rt.linear(c['x'], c['fmt'], c['g'], c['n'], codes, scales, out=c['y'], **kw)
+
+    out = {'cells': {}}
+    for c in cells:
+        plain = gemv_bytes(1, c['n'], c['k'], c['fmt'], c['g'], 0)
+        reps = min(512, -(-300_000_000 // plain))
+        w = (torch.randn(c['n'], c['k'], generator=gen) * 0.02).half().to(device)
+        packed = [rt.quantize_pack(w, c['fmt'], c['g']) for _ in range(reps)]
+        row = {'replicas': reps}
+        for corr in (True, False):
+            us = graph_us([call(c, cs, sc, corr) for cs, sc in packed], reps)
+            nbytes = gemv_bytes(1, c['n'], c['k'], c['fmt'], c['g'], RANK if corr else 0)
+            row['corrected' if corr else 'plain'] = {'us': round(us, 2), 'GB_per_s': round(nbytes / us / 1e3, 1)}
+        out['cells'][f"{c['fmt']} g{c['g']} {c['n']}x{c['k']}"] = row
+        del packed, w
+    for corr in (True, False):
+        calls = [call(c, *c['reps'][r], corr) for r in range(REPLICAS) for c in cells]
+        us = graph_us(calls, REPLICAS)
+        nbytes = sum(gemv_bytes(1, c['n'], c['k'], c['fmt'], c['g'], RANK if corr else 0) for c in cells)
+        out['sweep_corrected' if corr else 'sweep_plain'] = {'us': round(us, 2), 'GB_per_s': round(nbytes / us / 1e3, 1)}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -877,9 +929,13 @@ def main():
     ap.add_argument('--profile', choices=['dominant', 'prefill', 'batched', 'attention', 'quantize', 'decode',
                                           'decode360'],
                     help='run a small fixed workload for an ncu capture and exit')
+    ap.add_argument('--cells', action='store_true',
+                    help='print the per-cell device time of the sweep, with and without corrections, and exit')
     args = ap.parse_args()
     if args.profile:
         return profile_case(args.profile)
+    if args.cells:
+        return cells_report()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == 'reference':
