@@ -67,7 +67,7 @@ def test_step_splits_at_all_reduces_and_replays_in_order(fakes):
         fakes.append(('kernels', 'head'))
         return 'logits'
 
-    rec = sm._PiecewiseGraph('cpu')
+    rec = sm._PiecewiseGraph()
     assert rec.record(step) == 'logits'
     assert sm._PiecewiseGraph.active is None
     assert [s[0] for s in rec.steps] == ['graph', 'all_reduce', 'graph', 'all_reduce', 'graph']
@@ -87,7 +87,7 @@ def test_error_inside_the_step_closes_the_capture(fakes):
         sm._all_reduce(torch.zeros(2), 'tp')
         raise RuntimeError('step failed')
 
-    rec = sm._PiecewiseGraph('cpu')
+    rec = sm._PiecewiseGraph()
     with pytest.raises(RuntimeError, match='step failed'):
         rec.record(step)
     assert sm._PiecewiseGraph.active is None

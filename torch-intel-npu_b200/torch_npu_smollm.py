@@ -18,7 +18,8 @@ What changes underneath the API:
 * ``SmolKVCache`` snapshots share one preallocated device buffer; decoding from a stale
   snapshot copies the buffer first, so snapshots stay immutable as in the reference.
 ``SmolForCausalLM`` (not in the reference) adds the tied embedding / LM head and a
-greedy ``generate`` whose decode step is one replayed CUDA graph.
+greedy ``generate`` whose decode step is one replayed CUDA graph (for a tensor-parallel
+stack, graphs split at the NCCL all-reduces, which run eagerly between them).
 """
 from dataclasses import dataclass, field
 import json
@@ -53,8 +54,7 @@ class _PiecewiseGraph:
 
     active = None   # the recorder in use while a step is being captured
 
-    def __init__(self, device):
-        self.device = device
+    def __init__(self):
         self.pool = torch.cuda.graph_pool_handle()
         self.steps = []
         self.graph = None
@@ -849,7 +849,7 @@ class SmolForCausalLM(torch.nn.Module):
             st['ids'].copy_(ids)
             if piecewise:
                 side.synchronize()
-                rec = _PiecewiseGraph(self.device)
+                rec = _PiecewiseGraph()
                 st['logits'] = rec.record(lambda: self._decode_step(st))
             else:
                 g = torch.cuda.CUDAGraph(keep_graph=True)   # kept for launch counting (cudaGraphGetNodes)
@@ -860,13 +860,6 @@ class SmolForCausalLM(torch.nn.Module):
             st['piecewise'] = rec
         else:
             st['graph'] = g
-
-    def release_graphs(self):
-        """Drop every captured decode graph (before destroying a tensor-parallel process group)."""
-        for st in self._graphs.values():
-            st['graph'] = None
-            st['piecewise'] = None
-            st['logits'] = None
 
     def generate(self, ids, steps, *, graph=True, return_logits=False):
         """Greedy decoding: prefill ``ids`` [B, S] (device int64), then ``steps`` tokens.
