@@ -114,6 +114,44 @@ def test_batch_shards_cover_every_sequence_once():
             assert max(e - s for s, e in spans) - min(e - s for s, e in spans) <= 1
 
 
+@pytest.mark.parametrize('world', [2, 4, 8])
+def test_configs4_layer_shards_at_every_scaling_world_size(world):
+    """configs[4] (SmolLM-1.7B: hidden 2048, 32 / 32 heads, FFN 8192, NF4 group 64) runs tensor
+    parallel at every world size of the benchmark's scaling run.  Its per-rank config keeps
+    whole 64-wide heads; every column-parallel projection (real N, a short K) splits into
+    row-byte ranges that concatenate to the whole packing; every row-parallel projection (real
+    K, a few rows) splits on group boundaries, each shard of the rank's local K."""
+    import smollm_parallel as sp
+    import torch_npu_smollm as sm
+    from torch_npu_lowbit import PackedWeight
+    config = dict(model_type='llama', hidden_size=2048, intermediate_size=8192, num_attention_heads=32,
+                  num_key_value_heads=32, rms_norm_eps=1e-5, rope_theta=10000.0, vocab_size=49152,
+                  num_hidden_layers=24)
+    local = sm.SmolConfig.from_dict({k: v for k, v in sp.tp_config(config, world).items() if k != 'tp_world'})
+    assert (local.heads * world, local.kv_heads * world, local.intermediate * world, local.head_dim) == (32, 32, 8192, 64)
+    full_shapes, local_shapes = sm.SmolConfig.from_dict(config).shapes(), local.shapes()
+    gen = torch.Generator().manual_seed(5)
+    for name, shape in full_shapes.items():
+        if len(shape) != 2:
+            continue
+        n, k = shape
+        if name in sp.COLUMN:
+            w = (torch.randn(n, 64, generator=gen) * 0.02).numpy()
+            g, data, scales = ref.quantize(w, 'nf4', 64)
+            q = PackedWeight((n, 64), 'nf4', g, data, scales)
+            shards = [sp.shard_packed_rows(q, r, world) for r in range(world)]
+            assert all(s.shape == (local_shapes[name][0], 64) for s in shards), name
+            assert b''.join(s.data for s in shards) == q.data and b''.join(s.scales for s in shards) == q.scales
+        else:
+            w = (torch.randn(4, k, generator=gen) * 0.02).numpy()
+            g, data, scales = ref.quantize(w, 'nf4', 64)
+            q = PackedWeight((4, k), 'nf4', g, data, scales)
+            shards = [sp.shard_packed_cols(q, r, world)[0] for r in range(world)]
+            assert all(s.shape == (4, local_shapes[name][1]) for s in shards), name
+            rows = [np.frombuffer(s.data, np.uint8).reshape(4, -1) for s in shards]
+            assert np.concatenate(rows, 1).tobytes() == q.data
+
+
 def _fail_worker(rank, world, port, results):
     _init(rank, world, port, timeout_s=5)
     t = torch.ones(4)
