@@ -28,9 +28,11 @@
 // projection z = half(x . V^T) comes from the launch before (z, lowrank_project_kernel) or,
 // for weights of >= 4 MiB (whose main loop outlasts it), from the first CTAs of the same
 // launch (zv): each reduces one K slice of x . V^T, fences its partials and counts its
-// arrival; after its main loop each CTA waits (bounded, LB_ERR_TIMEOUT in the status word on
-// expiry) for every slice and sums them in slice order.  That launch is used only when the
-// whole grid fits on the device at once, so the wait always ends.
+// arrival; the last to arrive publishes z as 32 words in the zeroed counter header.  After
+// its main loop a CTA takes those words, or sums the slices itself in slice order once all
+// have arrived (the same bits either way); the wait is bounded (LB_ERR_TIMEOUT in the
+// status word on expiry).  That launch is used only when the whole grid fits on the device
+// at once, so the wait always ends.
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
