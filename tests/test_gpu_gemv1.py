@@ -89,3 +89,21 @@ def test_one_row_gemv_settings(env):
     assert r.returncode == 0, r.stderr[-2000:]
     for case, (mx, mean, same) in zip(cases, json.loads(r.stdout.strip().splitlines()[-1])):
         assert mx <= TOL_MAX and mean <= TOL_MEAN and same, (env, case, mx, mean)
+
+
+ZSELF_SHAPES = [(16, 128), (576, 1536), (64, 2048), (32, 4096), (1536, 1536)]
+
+
+def test_one_row_gemv_cta_local_projection():
+    """LOWBIT_G1_ZSELF=1: below 4 MiB of codes every CTA computes the correction projection
+    itself from the activation row it staged (no projection launch, no wait between CTAs);
+    K = 4096 is the longest it takes, and 1536x1536 reads more V than it allows over all its
+    CTAs, so that call keeps the projection launch.  Same oracle tolerance, deterministic."""
+    cases = [[n, k, fmt, g, rank, bias] for n, k in ZSELF_SHAPES
+             for fmt, g in (('int4', 64), ('nf4', 64), ('int4', 128), ('nf4', 128))
+             for rank, bias in ((min(32, n), True), (5, False))]
+    r = subprocess.run([sys.executable, '-c', CHILD, str(ROOT), json.dumps(cases)], capture_output=True, text=True,
+                       timeout=600, env={**os.environ, 'LOWBIT_G1_ZSELF': '1'})
+    assert r.returncode == 0, r.stderr[-2000:]
+    for case, (mx, mean, same) in zip(cases, json.loads(r.stdout.strip().splitlines()[-1])):
+        assert mx <= TOL_MAX and mean <= TOL_MEAN and same, (case, mx, mean)

@@ -890,7 +890,8 @@ bool gemv1_supported(int fmt, int group, int m, int n, int k, const void *x, con
                      const void *up, int rank);
 cudaError_t launch_gemv1(int fmt, int group, int n, int k, const uint16_t *x, const uint8_t *codes,
                          const uint16_t *scales, const uint16_t *z, const uint16_t *down, const uint16_t *up, int rank,
-                         const uint16_t *bias, uint16_t *y, int *counters, float *zpart, int *err, cudaStream_t st);
+                         const uint16_t *bias, uint16_t *y, int *counters, float *zpart, int *err, cudaStream_t st,
+                         bool self_z);
 size_t gemv1_zpart_bytes();
 
 size_t gemv_workspace_bytes(int fmt, int m, int n, int k) {
@@ -1028,7 +1029,7 @@ cudaError_t launch_gemv(int fmt, int group, int m, int n, int k, const uint16_t 
   // one activation row of 4-bit codes: the one-row kernel (csrc/gemv1.cu)
   if (!resid && zs == 32 && rank <= 32 && gemv1_supported(fmt, group, m, n, k, x, codes, scales, z ? up : nullptr, rank))
     return launch_gemv1(fmt, group, n, k, x, codes, scales, z, nullptr, z ? up : nullptr, rank, bias, y, nullptr, nullptr,
-                        nullptr, st);
+                        nullptr, st, false);
   GemvParams p = {};
   p.m = m; p.n = n; p.k = k; p.group = fmt == LB_FMT_FP16 ? k : group;
   p.x = reinterpret_cast<const __half *>(x);
@@ -1089,9 +1090,16 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
       const char *v = getenv("LOWBIT_G1_FUSE_MIN");
       return v ? int64_t(atoll(v)) : kFuseZMinBytes;
     }();
-    if (int64_t(n) * k / 2 < g1_min || !zpart || !err) return cudaSuccess;
+    // LOWBIT_G1_ZSELF=1: below the threshold, every CTA computes z itself from its staged x
+    // (redundant V reads from L2, no wait between CTAs; refused for long K or many CTAs)
+    static const bool self_z = [] {
+      const char *v = getenv("LOWBIT_G1_ZSELF");
+      return v && v[0] == '1';
+    }();
+    const bool big = int64_t(n) * k / 2 >= g1_min;
+    if (big ? (!zpart || !err) : !self_z) return cudaSuccess;
     const cudaError_t e = launch_gemv1(fmt, group, n, k, x, codes, scales, nullptr, down, up, rank, bias, y, counters,
-                                       zpart, err, st);
+                                       zpart, err, st, !big);
     if (e == cudaErrorNotSupported) return cudaSuccess;
     *fused = true;
     return e;

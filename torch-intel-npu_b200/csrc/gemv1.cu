@@ -50,6 +50,8 @@ constexpr int kG1Done = kG1Counters - 3;   // in-launch projection: CTAs done wi
 constexpr int kG1ZArrive = kG1Counters - 2;   //   and slices arrived
 constexpr int kG1ZWords = kG1Done - 32;       //   and the projection's 32 words (0 = not written)
 constexpr int kG1MaxSlices = 32;
+constexpr int kG1SelfMaxK = 4096;           // CTA-local projection (zself): longest K
+constexpr int64_t kG1SelfMaxBytes = int64_t(8) << 20;   //   and most V bytes read over all CTAs
 
 struct Gemv1Params {
   int n, k;
@@ -72,6 +74,7 @@ struct Gemv1Params {
   int *err;              // status word (LB_ERR_TIMEOUT)
   long long wait_cycles;
   int z_extra;           // test hook: slice arrivals waited for beyond zx (0 in use)
+  int zself;             // 1: every main CTA computes z = half(x . V^T) from its staged x (zx = 0)
 };
 
 __device__ __forceinline__ int g1_ld_acquire(const int *p) {
@@ -439,6 +442,48 @@ __device__ __forceinline__ void g1_units(const Gemv1Params &p, int u0, int cnt, 
   }
 }
 
+// z = half(x . V^T) by one main CTA from the activation row it staged (p.zself): thread t
+// owns rank t / W and the x chunks (t % W) + W j, whose products it adds in chunk order
+// (V loads issued 8 chunks at a time before the products); the W threads of a rank (lanes of
+// one warp) are then summed by shuffles.  INT4 stages x with each 8-chunk permuted
+// ([x0 x4 x2 x6 x1 x5 x3 x7]); V's chunk takes the same permutation.  zs[32]: the fp32
+// values of the halves (0 past the rank).
+template <bool kPermuted, int W>
+__device__ __forceinline__ void g1_z_self(const Gemv1Params &p, const uint8_t *xs, float *zs) {
+  constexpr int kB = 8;
+  const int r = threadIdx.x / W, sub = threadIdx.x % W;
+  const int chunks = p.k >> 3;
+  float acc = 0.f;
+  if (r < p.rank) {
+    const __half *vr = p.zv + int64_t(r) * p.k;
+    for (int c0 = sub; c0 < chunks; c0 += W * kB) {
+      uint4 v[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int ch = c0 + W * b;
+        v[b] = ch < chunks ? ldg_nc_v4(vr + 8 * ch) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int ch = c0 + W * b;
+        if (ch >= chunks) break;
+        const uint4 xv = *reinterpret_cast<const uint4 *>(xs + 16 * ch);
+        uint4 vv = v[b];
+        if constexpr (kPermuted)
+          vv = make_uint4(__byte_perm(v[b].x, v[b].z, 0x5410), __byte_perm(v[b].y, v[b].w, 0x5410),
+                          __byte_perm(v[b].x, v[b].z, 0x7632), __byte_perm(v[b].y, v[b].w, 0x7632));
+        fma2_f16_f32(acc, vv.x, xv.x);
+        fma2_f16_f32(acc, vv.y, xv.y);
+        fma2_f16_f32(acc, vv.z, xv.z);
+        fma2_f16_f32(acc, vv.w, xv.w);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (sub == 0) zs[r] = r < p.rank ? __half2float(__float2half_rn(acc)) : 0.f;
+}
+
 template <int FMT, int GS, int W>
 __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params p) {
   static_assert(FMT == LB_FMT_INT4 || FMT == LB_FMT_NF4, "4-bit codes only");
@@ -498,6 +543,12 @@ __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params
       u = e;
     }
   }
+  if (p.zself && threadIdx.x == 32) {
+    // this CTA's share of V (constant, like the codes) into L2 before the wait; every CTA reads all of it
+    const int64_t total = int64_t(p.rank) * p.k / 8;   // 16-byte chunks
+    const int64_t a = total * c / gridDim.x, b = total * (c + 1) / gridDim.x;
+    if (b > a) prefetch_l2_bulk(p.zv + 8 * a, uint32_t(16 * (b - a)));
+  }
   if (p.up && warp == W - 1 && lane == 0) {
     // the CTA's correction factor rows (as constant as the codes): in L2 for the epilogue
     const uint32_t bytes = uint32_t(nr) * 16u * uint32_t(p.rank) * 2u;
@@ -537,6 +588,9 @@ __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params
     }
   }
   __syncthreads();
+  float *zs = part + p.rmax * W * 16;   // [32] the projection
+  // the CTA's own projection, while the first weight loads are still in flight
+  if (p.zself) g1_z_self<!kNF4, W>(p, g1_smem + kLutBytes, zs);
 
   if (cnt > 0) {
     const uint32_t s_base = smem_u32(g1_smem);
@@ -550,8 +604,9 @@ __global__ void __launch_bounds__(32 * W, 16 / W) gemv1_kernel(const Gemv1Params
   const bool corr = p.up && (p.z || p.zv);
   uint4 u[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
   if (corr && p.rank == 32 && warp < nr) g1_load_u(p, rc0 + warp, u);
-  float *zs = part + p.rmax * W * 16;   // [32] the projection
-  if (p.zv) {
+  if (p.zself) {
+    // zs was written before the main loop (the barrier above orders it before the epilogues)
+  } else if (p.zv) {
     g1_collect_z(p, zs);
     // the CTA's done count from the last warp, off the path of the epilogues of warps < nr
     if (threadIdx.x == 32 * (W - 1)) g1_release_z(p);
@@ -684,7 +739,8 @@ extern std::atomic<int> g_z_extra;
 // workspace, counters: the header's arrival counters, err: its status word).
 cudaError_t launch_gemv1(int fmt, int group, int n, int k, const uint16_t *x, const uint8_t *codes,
                          const uint16_t *scales, const uint16_t *z, const uint16_t *down, const uint16_t *up, int rank,
-                         const uint16_t *bias, uint16_t *y, int *counters, float *zpart, int *err, cudaStream_t st) {
+                         const uint16_t *bias, uint16_t *y, int *counters, float *zpart, int *err, cudaStream_t st,
+                         bool self_z) {
   Gemv1Params p = {};
   p.n = n; p.k = k;
   p.kbs = k / 128;
@@ -695,7 +751,12 @@ cudaError_t launch_gemv1(int fmt, int group, int n, int k, const uint16_t *x, co
   p.bias = reinterpret_cast<const __half *>(bias);
   p.y = reinterpret_cast<__half *>(y);
   int zx = 0;
-  if (up && down) {
+  if (up && down && self_z) {
+    p.up = reinterpret_cast<const __half *>(up);
+    p.zv = reinterpret_cast<const __half *>(down);
+    p.rank = rank;
+    p.zself = 1;
+  } else if (up && down) {
     p.up = reinterpret_cast<const __half *>(up);
     p.zv = reinterpret_cast<const __half *>(down);
     p.rank = rank;
@@ -711,6 +772,9 @@ cudaError_t launch_gemv1(int fmt, int group, int n, int k, const uint16_t *x, co
     p.rank = rank;
   }
   const G1Plan pl = g1_plan(p.rgs, zx);
+  // the CTA-local projection: every CTA reads all of V from L2 and stages it 8 chunks per
+  // thread at a time, so it is taken for short K and a bounded total of those reads only
+  if (p.zself && (k > kG1SelfMaxK || int64_t(pl.ctas) * rank * k * 2 > kG1SelfMaxBytes)) return cudaErrorNotSupported;
   p.zx = zx;
   p.rq = pl.rq;
   p.rr = pl.rr;
