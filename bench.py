@@ -151,7 +151,8 @@ def launches_per_step(cells):
     with >= 4 MiB of codes computes its z projection inside the same launch (the rule of
     launch_gemv_fused_z in csrc/gemv.cu, for the one-row kernel of csrc/gemv1.cu as for the
     general one; the sweep's grids always fit the device at once); otherwise the projection
-    is a launch of its own."""
+    is a launch of its own.  The count follows the default settings: LOWBIT_G1_FUSE_MIN and
+    LOWBIT_G1_ZSELF change which cells fuse their projection."""
     import lowbit_runtime as rt
     count = 0
     for c in cells:

@@ -1084,8 +1084,8 @@ cudaError_t launch_gemv_fused_z(int fmt, int group, int m, int n, int k, const u
   *fused = false;
   if (rank >= 1 && rank <= 32 && gemv1_supported(fmt, group, m, n, k, x, codes, scales, up, rank)) {
     // the one-row kernel (csrc/gemv1.cu): the projection in the same launch from >= 4 MiB of
-    // codes (measured on B200: equal or faster there; below it the projection's own launch
-    // is faster), unless the grid could not be resident at once
+    // codes (slice CTAs; measured on B200: faster there, while below it the projection's own
+    // launch is faster), unless the grid could not be resident at once
     static const int64_t g1_min = [] {   // LOWBIT_G1_FUSE_MIN: the threshold in code bytes (comparison)
       const char *v = getenv("LOWBIT_G1_FUSE_MIN");
       return v ? int64_t(atoll(v)) : kFuseZMinBytes;
